@@ -1,0 +1,395 @@
+"""Tensor-level wrappers over the C ABI (PyTorch is only the plumbing here).
+
+Each function validates shapes the way the reference's ``check()`` does
+(``ValueError`` with the reference's message where one exists,
+src/barellm/utils.py:1-3) and then enqueues the CUDA kernels on the current
+stream.  Nothing falls back to a CPU or ATen implementation: on a CPU tensor,
+or without the built library, every call raises.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _native as nat
+
+DTYPE_CODE = {torch.float32: nat.BL_F32, torch.float16: nat.BL_F16, torch.bfloat16: nat.BL_BF16}
+
+
+class KernelError(RuntimeError):
+    """A CUDA launch or driver call inside the library failed."""
+
+
+def _check(cond: bool, message: str) -> None:
+    if not cond:
+        raise ValueError(message)
+
+
+def _raise_rc(rc: int) -> None:
+    if rc == nat.BL_OK:
+        return
+    msg = nat.last_error()
+    if rc == nat.BL_ERR_LAUNCH:
+        raise KernelError(msg)
+    raise ValueError(msg)
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(t: torch.Tensor, name: str) -> None:
+    if not t.is_cuda:
+        raise RuntimeError(
+            f"barellm_b200 kernels run on CUDA devices only; {name} is on {t.device}"
+        )
+
+
+def _int32_on(t: torch.Tensor, device: torch.device, name: str) -> torch.Tensor:
+    _check(t.dtype == torch.int32, f"{name} must be int32")
+    _check(t.device == device, f"{name} must be on {device}")
+    return t
+
+
+def _paged_layer(
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    layer: int,
+    block_tables: torch.Tensor,
+    row_ids: torch.Tensor | None,
+) -> nat.PagedLayer:
+    _require_cuda(key_cache, "key_cache")
+    _check(key_cache.ndim == 5, "K/V pool must have shape [L, P, H, S, D]")
+    _check(key_cache.shape == value_cache.shape, "K/V pools must have identical shape")
+    _check(key_cache.dtype == value_cache.dtype, "K/V dtype must match")
+    _check(key_cache.device == value_cache.device, "K/V device must match")
+    _check(key_cache.is_contiguous() and value_cache.is_contiguous(), "K/V pools must be contiguous")
+    _check(key_cache.dtype in DTYPE_CODE, f"unsupported dtype {key_cache.dtype}")
+    num_layers = key_cache.shape[0]
+    if not 0 <= layer < num_layers:
+        raise IndexError(f"Invalid layer index: {layer}")
+    _int32_on(block_tables, key_cache.device, "block_tables")
+    _check(block_tables.ndim == 2 and block_tables.stride(1) == 1, "block_tables must be [rows, width] with unit inner stride")
+    _check(block_tables.shape[1] > 0, "block_tables must have at least one column")
+    if row_ids is not None:
+        _int32_on(row_ids, key_cache.device, "row_ids")
+    pl = nat.PagedLayer()
+    pl.k_pool = key_cache.data_ptr()
+    pl.v_pool = value_cache.data_ptr()
+    pl.num_layers, pl.num_blocks, pl.num_kv_heads, pl.block_size, pl.head_dim = key_cache.shape
+    pl.dtype = DTYPE_CODE[key_cache.dtype]
+    pl.layer = layer
+    pl.block_tables = block_tables.data_ptr()
+    pl.bt_stride = block_tables.stride(0)
+    pl.bt_width = block_tables.shape[1]
+    pl.row_ids = _ptr(row_ids)
+    return pl
+
+
+def paged_append(
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    layer: int,
+    block_tables: torch.Tensor,
+    start_pos: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    *,
+    row_ids: torch.Tensor | None = None,
+    new_offsets: torch.Tensor | None = None,
+    max_new_tokens: int | None = None,
+    err: torch.Tensor | None = None,
+) -> None:
+    """Writes new K/V tokens straight into their pool slots.
+
+    ``key``/``value``: ``[B, Hkv, T, D]`` (any strides, D contiguous); row b's
+    tokens go to positions ``start_pos[b] ..``.  With ``new_offsets`` (``[B+1]``)
+    the tokens are packed on the T axis of a ``[1, Hkv, sum T, D]`` tensor.
+    Mirrors PagedLayerKV.append_only, src/barellm/engine/paged_kv_cache.py:151-193.
+    """
+    pl = _paged_layer(key_cache, value_cache, layer, block_tables, row_ids)
+    _check(key.ndim == 4 and value.ndim == 4, "K/V must have shape [B, H, T, D]")
+    _check(key.shape == value.shape, "K/V must have identical shape")
+    _check(key.stride() == value.stride(), "K/V must have identical strides")
+    _check(key.shape[1] == key_cache.shape[2], "KV-head count cannot change")
+    _check(key.shape[2] > 0, "K/V sequence length must be greater than zero")
+    _check(key.shape[3] == key_cache.shape[4], "Head dimension cannot change")
+    _check(key.dtype == key_cache.dtype, "K/V dtype cannot change")
+    _check(key.device == key_cache.device, "K/V device cannot change")
+    _check(key.dtype == value.dtype, "K/V dtype must match")
+    _check(key.stride(3) == 1, "K/V head_dim must be contiguous")
+    _int32_on(start_pos, key.device, "start_pos")
+    batch = start_pos.shape[0]
+    if new_offsets is None:
+        _check(key.shape[0] == batch, "batch size must match number of caches")
+        max_new = key.shape[2]
+    else:
+        _int32_on(new_offsets, key.device, "new_offsets")
+        _check(key.shape[0] == 1 and new_offsets.shape[0] == batch + 1, "packed K/V need [1, H, T, D] and [B+1] offsets")
+        _check(max_new_tokens is not None and max_new_tokens > 0, "packed append needs max_new_tokens")
+        max_new = int(max_new_tokens)
+    a = nat.AppendArgs()
+    a.kv = pl
+    a.k_new = key.data_ptr()
+    a.v_new = value.data_ptr()
+    # packed rows are addressed by new_offsets alone
+    a.new_stride_b = key.stride(0) if new_offsets is None else 0
+    a.new_stride_h = key.stride(1)
+    a.new_stride_t = key.stride(2)
+    a.start_pos = start_pos.data_ptr()
+    a.new_offsets = _ptr(new_offsets)
+    a.batch = batch
+    a.max_new_tokens = max_new
+    a.err = _ptr(err)
+    _raise_rc(nat.load().bl_paged_append(a, _stream(key.device)))
+
+
+def paged_gather(
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    layer: int,
+    block_tables: torch.Tensor,
+    seq_lens: torch.Tensor,
+    max_len: int,
+    *,
+    row_ids: torch.Tensor | None = None,
+    out: tuple[torch.Tensor, torch.Tensor] | None = None,
+    zero_fill: bool = True,
+    err: torch.Tensor | None = None,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Dense ``[B, Hkv, max_len, D]`` copy of the cached tokens, zero padded.
+
+    Mirrors PagedLayerKV.read + BatchLayerKV._pad
+    (src/barellm/engine/paged_kv_cache.py:215-240, batched_kv_cache.py:80-95).
+    """
+    pl = _paged_layer(key_cache, value_cache, layer, block_tables, row_ids)
+    _int32_on(seq_lens, key_cache.device, "seq_lens")
+    _check(max_len > 0, "KV cache is empty")
+    batch = seq_lens.shape[0]
+    hkv, d = key_cache.shape[2], key_cache.shape[4]
+    if out is None:
+        shape = (batch, hkv, max_len, d)
+        k_out = torch.empty(shape, dtype=key_cache.dtype, device=key_cache.device)
+        v_out = torch.empty_like(k_out)
+    else:
+        k_out, v_out = out
+        _check(k_out.shape == (batch, hkv, max_len, d) and v_out.shape == k_out.shape, "gather output shape mismatch")
+        _check(k_out.stride() == v_out.stride() and k_out.stride(3) == 1, "gather outputs need identical strides, D contiguous")
+    a = nat.GatherArgs()
+    a.kv = pl
+    a.seq_lens = seq_lens.data_ptr()
+    a.batch = batch
+    a.k_out = k_out.data_ptr()
+    a.v_out = v_out.data_ptr()
+    a.out_stride_b, a.out_stride_h, a.out_stride_t = k_out.stride(0), k_out.stride(1), k_out.stride(2)
+    a.max_len = max_len
+    a.zero_fill = 1 if zero_fill else 0
+    a.err = _ptr(err)
+    _raise_rc(nat.load().bl_paged_gather(a, _stream(key_cache.device)))
+    return k_out, v_out
+
+
+def decode_workspace_bytes(batch: int, num_q_heads: int, head_dim: int, block_size: int, max_seq_len: int) -> int:
+    return int(nat.load().bl_paged_decode_workspace_bytes(batch, num_q_heads, head_dim, block_size, max_seq_len))
+
+
+_WORKSPACES: dict[int, torch.Tensor] = {}
+
+
+def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Per-device scratch buffer for split-K decode (grown, never shrunk).
+
+    Calls on one device share it, so decode calls must be ordered on a single
+    stream (which the engine guarantees)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    ws = _WORKSPACES.get(idx)
+    if ws is None or ws.numel() < nbytes:
+        size = max(nbytes, 1 << 20)
+        if ws is not None:
+            size = max(size, 2 * ws.numel())
+        ws = torch.empty(size, dtype=torch.uint8, device=torch.device("cuda", idx))
+        _WORKSPACES[idx] = ws
+    return ws
+
+
+def _decode_args(
+    q: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    layer: int,
+    block_tables: torch.Tensor,
+    seq_lens: torch.Tensor,
+    max_seq_len: int,
+    scale: float | None,
+    out: torch.Tensor | None,
+    row_ids: torch.Tensor | None,
+    ws: torch.Tensor | None,
+    plan_ready: bool,
+    err: torch.Tensor | None,
+) -> tuple[nat.DecodeArgs, torch.Tensor, torch.Tensor]:
+    pl = _paged_layer(key_cache, value_cache, layer, block_tables, row_ids)
+    _require_cuda(q, "q")
+    if q.ndim == 4:
+        _check(q.shape[2] == 1, "decode takes one query token per request")
+        q3 = q[:, :, 0, :]
+    else:
+        q3 = q
+    _check(q3.ndim == 3, "q must be [B, Hq, D] or [B, Hq, 1, D]")
+    _check(q3.dtype == key_cache.dtype and q3.device == key_cache.device, "q must match the K/V pool dtype and device")
+    _check(q3.shape[2] == key_cache.shape[4], "Head dimension cannot change")
+    _check(q3.stride(2) == 1, "q head_dim must be contiguous")
+    _int32_on(seq_lens, q3.device, "seq_lens")
+    batch, hq, d = q3.shape
+    _check(seq_lens.shape[0] == batch, "batch size must match number of caches")
+    _check(hq % key_cache.shape[2] == 0, "num_heads must divide evenly by num_kv_heads")
+    if out is None:
+        out = torch.empty((batch, hq, d), dtype=q3.dtype, device=q3.device)
+    out3 = out[:, :, 0, :] if out.ndim == 4 else out
+    _check(out3.shape == (batch, hq, d) and out3.stride(2) == 1, "decode output must be [B, Hq, D], D contiguous")
+    nbytes = decode_workspace_bytes(batch, hq, d, key_cache.shape[3], max_seq_len)
+    if ws is None:
+        ws = workspace(q3.device, nbytes)
+    a = nat.DecodeArgs()
+    a.kv = pl
+    a.q = q3.data_ptr()
+    a.q_stride_b, a.q_stride_h = q3.stride(0), q3.stride(1)
+    a.out = out3.data_ptr()
+    a.out_stride_b, a.out_stride_h = out3.stride(0), out3.stride(1)
+    a.seq_lens = seq_lens.data_ptr()
+    a.batch = batch
+    a.num_q_heads = hq
+    a.scale = 1.0 / math.sqrt(d) if scale is None else float(scale)
+    a.workspace = ws.data_ptr()
+    a.workspace_bytes = ws.numel() * ws.element_size()
+    a.max_seq_len = max_seq_len
+    a.plan_ready = 1 if plan_ready else 0
+    a.err = _ptr(err)
+    return a, out, ws
+
+
+def paged_decode_plan(
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    block_tables: torch.Tensor,
+    seq_lens: torch.Tensor,
+    max_seq_len: int,
+    num_q_heads: int,
+    *,
+    row_ids: torch.Tensor | None = None,
+    ws: torch.Tensor | None = None,
+    err: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Builds the split-K plan for ``seq_lens`` once; reusable by every layer."""
+    batch = seq_lens.shape[0]
+    d = key_cache.shape[4]
+    q_dummy = torch.empty((batch, num_q_heads, d), dtype=key_cache.dtype, device=key_cache.device)
+    a, _, ws = _decode_args(q_dummy, key_cache, value_cache, 0, block_tables, seq_lens, max_seq_len, None,
+                            q_dummy, row_ids, ws, False, err)
+    _raise_rc(nat.load().bl_paged_decode_plan(a, _stream(key_cache.device)))
+    return ws
+
+
+def paged_decode(
+    q: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    layer: int,
+    block_tables: torch.Tensor,
+    seq_lens: torch.Tensor,
+    max_seq_len: int,
+    *,
+    scale: float | None = None,
+    out: torch.Tensor | None = None,
+    row_ids: torch.Tensor | None = None,
+    ws: torch.Tensor | None = None,
+    plan_ready: bool = False,
+    err: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """One-token GQA attention over paged K/V, read in place; returns ``[B, Hq, D]``.
+
+    Equals the reference decode chain read -> _pad -> repeat_interleave ->
+    attention_mask -> SDPA (src/barellm/attention/backend.py:34-61).
+    ``seq_lens`` are post-append lengths (>= 1), ``max_seq_len`` a host-side
+    upper bound used only to size the split-K workspace.
+    """
+    a, out, _ = _decode_args(q, key_cache, value_cache, layer, block_tables, seq_lens, max_seq_len, scale,
+                             out, row_ids, ws, plan_ready, err)
+    _raise_rc(nat.load().bl_paged_decode(a, _stream(key_cache.device)))
+    return out
+
+
+def paged_prefill(
+    q: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    layer: int,
+    block_tables: torch.Tensor,
+    seq_lens: torch.Tensor,
+    *,
+    q_offsets: torch.Tensor | None = None,
+    max_q_len: int | None = None,
+    scale: float | None = None,
+    out: torch.Tensor | None = None,
+    row_ids: torch.Tensor | None = None,
+    err: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Causal attention of new queries over prefix + themselves, read in place.
+
+    ``q``: ``[B, Hq, T, D]`` (any strides, D contiguous), or ``[1, Hq, sum C, D]``
+    packed with ``q_offsets`` ``[B+1]``.  ``seq_lens`` are the total lengths
+    after the append; query i of a row with C queries sees keys
+    ``0 .. seq_len - C + i``.  Returns a tensor shaped like ``q`` whose memory is
+    ``[B, T, Hq, D]`` (so ``out.transpose(1, 2).reshape(B, T, -1)`` is free).
+    """
+    pl = _paged_layer(key_cache, value_cache, layer, block_tables, row_ids)
+    _require_cuda(q, "q")
+    _check(q.ndim == 4, "q must be [B, Hq, T, D]")
+    _check(q.dtype == key_cache.dtype and q.device == key_cache.device, "q must match the K/V pool dtype and device")
+    _check(q.shape[3] == key_cache.shape[4], "Head dimension cannot change")
+    _check(q.shape[2] > 0, "K/V sequence length must be greater than zero")
+    _check(q.stride(3) == 1, "q head_dim must be contiguous")
+    _check(q.shape[1] % key_cache.shape[2] == 0, "num_heads must divide evenly by num_kv_heads")
+    _int32_on(seq_lens, q.device, "seq_lens")
+    batch = seq_lens.shape[0]
+    if q_offsets is None:
+        _check(q.shape[0] == batch, "batch size must match number of caches")
+        mq = q.shape[2]
+    else:
+        _int32_on(q_offsets, q.device, "q_offsets")
+        _check(q.shape[0] == 1 and q_offsets.shape[0] == batch + 1, "packed queries need [1, Hq, T, D] and [B+1] offsets")
+        _check(max_q_len is not None and max_q_len > 0, "packed prefill needs max_q_len")
+        mq = int(max_q_len)
+    if out is None:
+        b0, hq, t, d = q.shape
+        out = torch.empty((b0, t, hq, d), dtype=q.dtype, device=q.device).transpose(1, 2)
+    _check(out.shape == q.shape and out.stride(3) == 1, "prefill output must match q's shape, D contiguous")
+    a = nat.PrefillArgs()
+    a.kv = pl
+    a.q = q.data_ptr()
+    packed = q_offsets is not None  # packed rows are addressed by q_offsets alone
+    a.q_stride_b, a.q_stride_h, a.q_stride_t = (0 if packed else q.stride(0)), q.stride(1), q.stride(2)
+    a.out = out.data_ptr()
+    a.out_stride_b, a.out_stride_h, a.out_stride_t = (0 if packed else out.stride(0)), out.stride(1), out.stride(2)
+    a.q_offsets = _ptr(q_offsets)
+    a.seq_lens = seq_lens.data_ptr()
+    a.batch = batch
+    a.num_q_heads = q.shape[1]
+    a.max_q_len = mq
+    a.scale = 1.0 / math.sqrt(q.shape[3]) if scale is None else float(scale)
+    a.err = _ptr(err)
+    _raise_rc(nat.load().bl_paged_prefill(a, _stream(q.device)))
+    return out
+
+
+def decode_path(dtype: torch.dtype, head_dim: int, block_size: int, num_q_heads: int, num_kv_heads: int) -> int:
+    return int(nat.load().bl_decode_path(DTYPE_CODE[dtype], head_dim, block_size, num_q_heads, num_kv_heads))
+
+
+def prefill_path(dtype: torch.dtype, head_dim: int, block_size: int, num_q_heads: int, num_kv_heads: int) -> int:
+    return int(nat.load().bl_prefill_path(DTYPE_CODE[dtype], head_dim, block_size, num_q_heads, num_kv_heads))

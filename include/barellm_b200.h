@@ -1,0 +1,231 @@
+/*
+ * barellm_b200 — C ABI of the B200 (sm_100a) paged-KV hot path.
+ *
+ * The reference (quanhua92/barellm, pure Python on PyTorch) has no native
+ * code.  Each entry point below replaces a chain of ATen ops inside one of its
+ * Python methods; the replaced method is cited beside each declaration.
+ *
+ * Conventions
+ *   - Plain C: raw device pointers, int64 sizes/strides counted in ELEMENTS,
+ *     a CUDA stream passed as `void*` (a cudaStream_t; NULL = legacy stream).
+ *   - Every call validates its arguments on the host, enqueues kernels on the
+ *     stream and returns without synchronising.  Return value 0 = BL_OK; any
+ *     other value is one of BL_ERR_*, and bl_last_error() (thread-local)
+ *     holds a one-line message.
+ *   - Nothing here allocates device memory.  Scratch space for split-K decode
+ *     is a caller-owned workspace sized by bl_paged_decode_workspace_bytes().
+ *   - Device-side faults are never raised.  A block id outside [0, P) or a
+ *     block-table column outside the table width makes the kernel skip that
+ *     access and OR a BL_DEVERR_* bit into the caller's `err` word (a device
+ *     int32, may be NULL).  Every wait inside a kernel is bounded; a wait that
+ *     runs out sets BL_DEVERR_TIMEOUT and the kernel returns.
+ *
+ * Paged pool layout (identical to the reference's PagedKVCache tensors,
+ * src/barellm/engine/paged_kv_cache.py:66-74):
+ *   k_pool, v_pool : [num_layers, num_blocks, num_kv_heads, block_size, head_dim]
+ *   contiguous, element type `dtype`.
+ * Block tables (reference PagedBatchKVMetadata.block_tables,
+ * src/barellm/engine/batched_kv_cache.py:124-132): int32, row r holds the
+ * physical block of logical block j at block_tables[r * bt_stride + j] for
+ * j < bt_width.  Request b uses row row_ids[b] (row_ids may be NULL: row b).
+ */
+#ifndef BARELLM_B200_H
+#define BARELLM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BL_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define BL_API __attribute__((visibility("default")))
+#else
+#define BL_API
+#endif
+
+/* return codes */
+enum {
+  BL_OK = 0,
+  BL_ERR_ARG = 1,         /* bad shape, stride, pointer or size           */
+  BL_ERR_DTYPE = 2,       /* unsupported element type                      */
+  BL_ERR_CAPACITY = 3,    /* workspace or index range too small            */
+  BL_ERR_LAUNCH = 4,      /* a CUDA launch or driver call failed           */
+  BL_ERR_UNSUPPORTED = 5  /* valid request this build does not implement   */
+};
+
+/* element types */
+enum { BL_F32 = 0, BL_F16 = 1, BL_BF16 = 2 };
+
+/* bits OR-ed into the device error word */
+enum {
+  BL_DEVERR_BLOCK_ID = 1,   /* physical block id outside [0, num_blocks)        */
+  BL_DEVERR_TABLE = 2,      /* logical block beyond the block-table width       */
+  BL_DEVERR_TIMEOUT = 4,    /* a bounded wait inside a kernel ran out           */
+  BL_DEVERR_WORKSPACE = 8   /* the decode plan needs more units than allocated  */
+};
+
+/* One layer of a paged K/V pool plus the block tables that index it. */
+typedef struct bl_paged_layer {
+  void* k_pool;
+  void* v_pool;
+  int64_t num_layers;
+  int64_t num_blocks;
+  int64_t num_kv_heads;
+  int64_t block_size;
+  int64_t head_dim;
+  int32_t dtype;  /* BL_F32 / BL_F16 / BL_BF16 */
+  int32_t layer;  /* which layer slice of the pool */
+  const int32_t* block_tables;
+  int64_t bt_stride;
+  int64_t bt_width;
+  const int32_t* row_ids; /* [batch] or NULL */
+} bl_paged_layer;
+
+/* ------------------------------------------------------------------------ */
+/* Append: slot-mapped K/V scatter into the pool.                            */
+/* Replaces PagedLayerKV.append_only (src/barellm/engine/paged_kv_cache.py:  */
+/* 151-193) and its per-row loop BatchLayerKV.append_only                    */
+/* (src/barellm/engine/batched_kv_cache.py:40-63).                           */
+/*                                                                          */
+/* Token t (0-based) of request b, head h, lives at                         */
+/*   k_new + b*new_stride_b + (o_b + t)*new_stride_t + h*new_stride_h       */
+/* where o_b = new_offsets[b] (ragged, packed along the token axis) or 0.   */
+/* Row b appends n_b tokens: new_offsets[b+1]-new_offsets[b], or            */
+/* max_new_tokens when new_offsets is NULL.  They go to logical positions   */
+/* start_pos[b] .. start_pos[b]+n_b-1.  The last axis (head_dim) must be    */
+/* contiguous.  The copy is bit-exact.                                      */
+typedef struct bl_append_args {
+  bl_paged_layer kv;
+  const void* k_new;
+  const void* v_new;
+  int64_t new_stride_b;
+  int64_t new_stride_h;
+  int64_t new_stride_t;
+  const int32_t* start_pos;   /* [batch], device */
+  const int32_t* new_offsets; /* [batch+1], device, or NULL */
+  int64_t batch;
+  int64_t max_new_tokens;
+  int32_t* err;               /* device int32 or NULL */
+} bl_append_args;
+
+BL_API int bl_paged_append(const bl_append_args* args, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Gather: dense read of pages, with optional zero padding.                  */
+/* Replaces PagedLayerKV.read (src/barellm/engine/paged_kv_cache.py:215-240) */
+/* and BatchLayerKV.read/_pad (src/barellm/engine/batched_kv_cache.py:65-95).*/
+/* Writes out[b, h, t, :] for t < max_len: the cached token when             */
+/* t < seq_lens[b], else zeros when zero_fill != 0 (left untouched if 0).    */
+typedef struct bl_gather_args {
+  bl_paged_layer kv;
+  const int32_t* seq_lens; /* [batch], device */
+  int64_t batch;
+  void* k_out;
+  void* v_out;
+  int64_t out_stride_b;
+  int64_t out_stride_h;
+  int64_t out_stride_t;
+  int64_t max_len;
+  int32_t zero_fill;
+  int32_t* err;
+} bl_gather_args;
+
+BL_API int bl_paged_gather(const bl_gather_args* args, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Decode attention: one query token per request, GQA, read in place.        */
+/* Replaces gather + pad + repeat_interleave + padding mask + SDPA in        */
+/* SDPAAttentionBackend.attend (src/barellm/attention/backend.py:34-61) for  */
+/* the batched decode path (src/barellm/engine/engine.py:458-488).           */
+/*                                                                          */
+/* out[b, hq, :] = softmax(scale * q[b,hq,:] . K[b, hq/G, t, :]) V           */
+/* over t < seq_lens[b] (post-append lengths, >= 1), G = Hq / Hkv.           */
+/* Long rows are split into fixed 512-token chunks whose partial results    */
+/* are merged by a separate reduce kernel; the split depends only on the    */
+/* row's own length, so a row's result does not depend on the batch.       */
+typedef struct bl_decode_args {
+  bl_paged_layer kv;
+  const void* q;
+  int64_t q_stride_b;
+  int64_t q_stride_h;
+  void* out;
+  int64_t out_stride_b;
+  int64_t out_stride_h;
+  const int32_t* seq_lens; /* [batch], device */
+  int64_t batch;
+  int64_t num_q_heads;
+  float scale;
+  void* workspace;          /* device scratch, >= bl_paged_decode_workspace_bytes */
+  size_t workspace_bytes;
+  int64_t max_seq_len;      /* host upper bound on seq_lens[] */
+  int32_t plan_ready;       /* 1: workspace already holds the plan for these seq_lens */
+  int32_t* err;
+} bl_decode_args;
+
+BL_API size_t bl_paged_decode_workspace_bytes(int64_t batch, int64_t num_q_heads,
+                                       int64_t head_dim, int64_t block_size,
+                                       int64_t max_seq_len);
+
+/* Builds the split-K work plan for seq_lens into the workspace.  The plan
+ * depends only on seq_lens, so one plan serves every layer of a step. */
+BL_API int bl_paged_decode_plan(const bl_decode_args* args, void* stream);
+
+/* Runs the plan (built first unless plan_ready), the attention kernel and
+ * the split-K reduce kernel. */
+BL_API int bl_paged_decode(const bl_decode_args* args, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Prefill attention: causal attention of new query tokens over a paged      */
+/* prefix plus themselves, read in place.                                    */
+/* Replaces the prefill SDPA(is_causal=True) of SDPAAttentionBackend.attend  */
+/* (src/barellm/attention/backend.py:52-61) and generalises it to a          */
+/* non-empty prefix (chunked prefill), where query i of a row whose total    */
+/* length is L and query count is C attends keys 0 .. L-C+i (bottom-right    */
+/* aligned causal mask).                                                     */
+/*                                                                          */
+/* Query i of row b, head hq: q + b*q_stride_b + (o_b + i)*q_stride_t        */
+/*   + hq*q_stride_h, o_b = q_offsets[b] (packed) or 0; the row has C_b =    */
+/* q_offsets[b+1]-q_offsets[b] queries, or max_q_len when q_offsets is NULL. */
+/* `out` uses the same addressing with its own strides.                      */
+typedef struct bl_prefill_args {
+  bl_paged_layer kv;
+  const void* q;
+  int64_t q_stride_b;
+  int64_t q_stride_t;
+  int64_t q_stride_h;
+  void* out;
+  int64_t out_stride_b;
+  int64_t out_stride_t;
+  int64_t out_stride_h;
+  const int32_t* q_offsets; /* [batch+1], device, or NULL */
+  const int32_t* seq_lens;  /* [batch], device: prefix + C_b */
+  int64_t batch;
+  int64_t num_q_heads;
+  int64_t max_q_len;
+  float scale;
+  int32_t* err;
+} bl_prefill_args;
+
+BL_API int bl_paged_prefill(const bl_prefill_args* args, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Misc.                                                                     */
+BL_API const char* bl_last_error(void);
+BL_API int bl_abi_version(void);
+
+/* Which kernel variant a call with these shapes would use (for tests and the
+ * bench):  0 = generic SIMT kernel, 1 = TMA + tensor-core kernel. */
+BL_API int bl_decode_path(int32_t dtype, int64_t head_dim, int64_t block_size,
+                   int64_t num_q_heads, int64_t num_kv_heads);
+BL_API int bl_prefill_path(int32_t dtype, int64_t head_dim, int64_t block_size,
+                    int64_t num_q_heads, int64_t num_kv_heads);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BARELLM_B200_H */
