@@ -36,6 +36,8 @@ EXPORTED = (
     "bl_paged_decode_workspace_bytes",
     "bl_paged_decode_plan",
     "bl_paged_decode",
+    "bl_paged_decode_attention",
+    "bl_paged_decode_reduce",
     "bl_paged_prefill",
     "bl_last_error",
     "bl_abi_version",
@@ -166,8 +168,9 @@ def load() -> ctypes.CDLL:
     lib.bl_paged_decode_workspace_bytes.restype = c_size_t
     lib.bl_paged_decode_plan.argtypes = [POINTER(DecodeArgs), c_void_p]
     lib.bl_paged_decode_plan.restype = c_int
-    lib.bl_paged_decode.argtypes = [POINTER(DecodeArgs), c_void_p]
-    lib.bl_paged_decode.restype = c_int
+    for fn in (lib.bl_paged_decode, lib.bl_paged_decode_attention, lib.bl_paged_decode_reduce):
+        fn.argtypes = [POINTER(DecodeArgs), c_void_p]
+        fn.restype = c_int
     lib.bl_paged_prefill.argtypes = [POINTER(PrefillArgs), c_void_p]
     lib.bl_paged_prefill.restype = c_int
     lib.bl_last_error.argtypes = []

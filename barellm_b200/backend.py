@@ -1,0 +1,115 @@
+"""The CUDA attention backend: ``AttentionBackend.attend`` over paged K/V.
+
+Drop-in for the reference's backend seam (src/barellm/attention/backend.py:12-79):
+``attend(q, new_k, new_v, layer_cache, group_size)`` appends the new K/V to
+the layer cache and returns attention of ``q`` over the whole cached sequence,
+``[B, Hq, q_len, D]``.  Where the reference appends, gathers every page into a
+dense tensor, repeats it per query head and runs SDPA, this backend appends
+with one scatter kernel and attends straight from the pages:
+
+  * BatchLayerKV (batched decode, engine.py:458-488): one append kernel for
+    the batch, then the split-K decode kernels for q_len == 1 (the plan is
+    built once per step and reused by every layer), or the paged prefill
+    kernel for q_len > 1;
+  * PagedLayerKV (single-request prefill, engine.py:226-257, including a
+    non-empty prefix = chunked prefill): append, then paged prefill with the
+    bottom-right causal mask (equal to SDPA(is_causal=True) without a prefix);
+  * None (uncached full forward): the new K/V are paged into a scratch pool
+    and attended causally by the same prefill kernel.
+There is no CPU path: a CPU tensor or an unknown cache type raises.
+"""
+
+from __future__ import annotations
+
+from typing import Literal, Protocol
+
+import torch
+
+from . import ops
+from .batched_kv_cache import BatchLayerKV
+from .paged_kv_cache import PagedLayerKV, _i32, check
+
+AttentionBackendName = Literal["auto", "sdpa", "triton", "cuda"]
+
+
+class AttentionBackend(Protocol):
+    def attend(self, q: torch.Tensor, new_k: torch.Tensor, new_v: torch.Tensor, layer_cache,
+               group_size: int) -> torch.Tensor: ...
+
+
+class CudaPagedAttentionBackend:
+    """Paged append + attention on sm_100a kernels."""
+
+    def attend(self, q: torch.Tensor, new_k: torch.Tensor, new_v: torch.Tensor, layer_cache,
+               group_size: int) -> torch.Tensor:
+        check(q.ndim == 4 and new_k.ndim == 4, "q/K/V must have shape [B, H, T, D]")
+        check(q.shape[1] == new_k.shape[1] * group_size, "num_heads must divide evenly by num_kv_heads")
+        if isinstance(layer_cache, BatchLayerKV):
+            return self._batched(q, new_k, new_v, layer_cache)
+        if isinstance(layer_cache, PagedLayerKV):
+            return self._single(q, new_k, new_v, layer_cache)
+        if layer_cache is None:
+            return self._uncached(q, new_k, new_v)
+        raise TypeError(f"the cuda attention backend reads paged caches, not {type(layer_cache).__name__}")
+
+    def _batched(self, q, new_k, new_v, layer: BatchLayerKV) -> torch.Tensor:
+        meta = layer.append_only(new_k, new_v)
+        s = layer.storage()
+        idx = layer.layers[0].layer_idx
+        if q.shape[2] == 1:
+            serial = ops.plan_serial(s.device)
+            if meta.plan_ws is None or meta.plan_token != serial or meta.plan_heads != q.shape[1]:
+                meta.plan_ws = ops.paged_decode_plan(s.key_cache, s.value_cache, s.arena.table, meta.seq_lens,
+                                                     meta.max_seq_len, q.shape[1], row_ids=meta.rows, err=s.err)
+                meta.plan_token = ops.plan_serial(s.device)
+                meta.plan_heads = q.shape[1]
+            out = ops.paged_decode(q, s.key_cache, s.value_cache, idx, s.arena.table, meta.seq_lens,
+                                   meta.max_seq_len, row_ids=meta.rows, ws=meta.plan_ws, plan_ready=True, err=s.err)
+            return out.unsqueeze(2)
+        return ops.paged_prefill(q, s.key_cache, s.value_cache, idx, s.arena.table, meta.seq_lens,
+                                 row_ids=meta.rows, err=s.err)
+
+    def _single(self, q, new_k, new_v, layer: PagedLayerKV) -> torch.Tensor:
+        check(q.shape[0] == 1, "PagedKVCache currently supports batch size 1")
+        layer.append_only(new_k, new_v)
+        s = layer.storage
+        n = layer.seq_len
+        rows = _i32([layer._request.row], s.device)
+        seq = _i32([n], s.device)
+        if q.shape[2] == 1:
+            out = ops.paged_decode(q, s.key_cache, s.value_cache, layer.layer_idx, s.arena.table, seq, n,
+                                   row_ids=rows, err=s.err)
+            return out.unsqueeze(2)
+        return ops.paged_prefill(q, s.key_cache, s.value_cache, layer.layer_idx, s.arena.table, seq, row_ids=rows,
+                                 err=s.err)
+
+    def _uncached(self, q, new_k, new_v) -> torch.Tensor:
+        """Causal self-attention of a fresh sequence: page it into a scratch
+        pool (block_size 16 when head_dim allows the tensor-core path) and run
+        the prefill kernel with an empty prefix."""
+        b, hkv, t, d = new_k.shape
+        bs = 16
+        nb = -(-t // bs)
+        pool_shape = (1, b * nb, hkv, bs, d)
+        kc = torch.empty(pool_shape, dtype=new_k.dtype, device=new_k.device)
+        vc = torch.empty_like(kc)
+        table = torch.arange(b * nb, dtype=torch.int32, device=new_k.device).view(b, nb)
+        zeros = torch.zeros(b, dtype=torch.int32, device=new_k.device)
+        ops.paged_append(kc, vc, 0, table, zeros, new_k, new_v)
+        seq = torch.full((b,), t, dtype=torch.int32, device=new_k.device)
+        return ops.paged_prefill(q, kc, vc, 0, table, seq)
+
+
+def create_attention_backend(name: AttentionBackendName = "cuda", *, sdpa=None) -> AttentionBackend:
+    """Backend factory mirroring the reference's (backend.py:64-79), for the
+    one backend this package provides.  ``"cuda"`` and ``"auto"`` give the
+    paged CUDA backend; ``"sdpa"`` is the reference's own portable backend and
+    lives there."""
+    del sdpa
+    if name not in ("auto", "sdpa", "triton", "cuda"):
+        raise ValueError(f"Unknown attention backend: {name!r}")
+    if name == "triton":
+        raise RuntimeError("The Triton attention backend is not implemented; use attention_backend='cuda'")
+    if name == "sdpa":
+        raise ValueError("the 'sdpa' backend is the reference's portable backend; barellm_b200 provides 'cuda'")
+    return CudaPagedAttentionBackend()

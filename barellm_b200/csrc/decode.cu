@@ -624,25 +624,26 @@ size_t tc_smem_bytes(int g) {
 }
 
 template <typename T>
-int launch_tc(const bl_decode_args& a, const WsLayout& w, cudaStream_t s) {
+int launch_tc_attention(const bl_decode_args& a, const WsLayout& w, cudaStream_t s) {
   const int g = (int)(a.num_q_heads / a.kv.num_kv_heads);
   const size_t smem = tc_smem_bytes(g);
-  static bool attr_done[9] = {false};
+  static int occ_cache[9] = {0};
   static std::mutex mu;
+  int occ = 0;
   {
     std::lock_guard<std::mutex> lk(mu);
-    if (!attr_done[g]) {
+    if (occ_cache[g] == 0) {
       if (cudaFuncSetAttribute(decode_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)tc_smem_bytes(8)) != cudaSuccess) {
         set_error("decode: cudaFuncSetAttribute failed");
         return BL_ERR_LAUNCH;
       }
-      attr_done[g] = true;
+      int o = 0;
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, decode_tc_kernel<T>, kThreadsTC, smem);
+      occ_cache[g] = o < 1 ? 1 : o;
     }
+    occ = occ_cache[g];
   }
-  int occ = 0;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_tc_kernel<T>, kThreadsTC, smem);
-  if (occ < 1) occ = 1;
 
   const uint64_t rows = (uint64_t)a.kv.num_layers * a.kv.num_blocks * a.kv.num_kv_heads * kBS;
   CUtensorMap kmap, vmap;
@@ -660,7 +661,7 @@ int launch_tc(const bl_decode_args& a, const WsLayout& w, cudaStream_t s) {
   k.o_sh = a.out_stride_h;
   k.block_tables = a.kv.block_tables;
   k.bt_stride = a.kv.bt_stride;
-  k.bt_width = (int32_t)a.kv.bt_width;
+  k.bt_width = (int32_t)std::min<int64_t>(a.kv.bt_width, INT32_MAX);
   k.row_ids = a.kv.row_ids;
   k.seq_lens = a.seq_lens;
   k.hq = (int32_t)a.num_q_heads;
@@ -682,7 +683,12 @@ int launch_tc(const bl_decode_args& a, const WsLayout& w, cudaStream_t s) {
   const int64_t grid = std::min<int64_t>((int64_t)num_sms() * occ, item_bound);
   decode_tc_kernel<T><<<(unsigned)grid, kThreadsTC, smem, s>>>(k, kmap, vmap);
   BL_CHECK_LAUNCH("decode_tc_kernel");
+  return BL_OK;
+}
 
+template <typename T>
+int launch_tc_reduce(const bl_decode_args& a, const WsLayout& w, cudaStream_t s) {
+  char* ws = (char*)a.workspace;
   ReduceArgs r;
   r.out = a.out;
   r.o_sb = a.out_stride_b;
@@ -690,13 +696,13 @@ int launch_tc(const bl_decode_args& a, const WsLayout& w, cudaStream_t s) {
   r.seq_lens = a.seq_lens;
   r.bs = kBS;
   r.chunk_blocks = kChunkTokens / kBS;
-  r.bt_width = (int32_t)a.kv.bt_width;
+  r.bt_width = (int32_t)std::min<int64_t>(a.kv.bt_width, INT32_MAX);
   r.hq = (int32_t)a.num_q_heads;
   r.d = kD;
-  r.row_base = k.row_base;
-  r.ws_lse = k.ws_lse;
-  r.ws_o = k.ws_o;
-  r.max_units = k.max_units;
+  r.row_base = (const int32_t*)(ws + w.row_base);
+  r.ws_lse = (const float*)(ws + w.lse);
+  r.ws_o = (const float*)(ws + w.o);
+  r.max_units = (int32_t)w.max_units;
   decode_reduce_kernel<T><<<dim3((unsigned)a.batch, (unsigned)a.num_q_heads), kD, 0, s>>>(r);
   BL_CHECK_LAUNCH("decode_reduce_kernel");
   return BL_OK;
@@ -792,33 +798,72 @@ extern "C" int bl_paged_decode_plan(const bl_decode_args* args, void* stream) {
   return BL_OK;
 }
 
-extern "C" int bl_paged_decode(const bl_decode_args* args, void* stream) {
-  int rc = check_decode(args, "bl_paged_decode");
+namespace bl {
+namespace {
+
+// Validates the tensor-core-path specifics and the workspace; fills `w`.
+int check_tc(const bl_decode_args& a, WsLayout& w) {
+  const uint64_t rows = (uint64_t)a.kv.num_layers * a.kv.num_blocks * a.kv.num_kv_heads * kBS;
+  BL_CHECK_ARG(rows <= (uint64_t)INT32_MAX, "bl_paged_decode: pool has more than 2^31 rows");
+  BL_CHECK_ARG(((uintptr_t)a.kv.k_pool & 15) == 0 && ((uintptr_t)a.kv.v_pool & 15) == 0,
+               "bl_paged_decode: pools must be 16-byte aligned");
+  BL_CHECK_ARG(((uintptr_t)a.q & 3) == 0 && a.q_stride_b % 2 == 0 && a.q_stride_h % 2 == 0,
+               "bl_paged_decode: q must be 4-byte aligned with even strides");
+  w = ws_layout(a.batch, a.num_q_heads, a.kv.head_dim, a.kv.block_size, a.max_seq_len);
+  if (!a.workspace || a.workspace_bytes < w.total) {
+    set_error("bl_paged_decode: workspace too small (%zu < %zu bytes)", a.workspace_bytes, w.total);
+    return BL_ERR_CAPACITY;
+  }
+  return BL_OK;
+}
+
+bool is_tc(const bl_decode_args& a) {
+  return tc_path(a.kv.dtype, a.kv.head_dim, a.kv.block_size, a.num_q_heads, a.kv.num_kv_heads);
+}
+
+}  // namespace
+}  // namespace bl
+
+extern "C" int bl_paged_decode_attention(const bl_decode_args* args, void* stream) {
+  int rc = check_decode(args, "bl_paged_decode_attention");
   if (rc) return rc;
   const bl_decode_args& a = *args;
   cudaStream_t s = (cudaStream_t)stream;
-  if (tc_path(a.kv.dtype, a.kv.head_dim, a.kv.block_size, a.num_q_heads, a.kv.num_kv_heads)) {
-    const uint64_t rows = (uint64_t)a.kv.num_layers * a.kv.num_blocks * a.kv.num_kv_heads * kBS;
-    BL_CHECK_ARG(rows <= (uint64_t)INT32_MAX, "bl_paged_decode: pool has more than 2^31 rows");
-    BL_CHECK_ARG(((uintptr_t)a.kv.k_pool & 15) == 0 && ((uintptr_t)a.kv.v_pool & 15) == 0,
-                 "bl_paged_decode: pools must be 16-byte aligned");
-    BL_CHECK_ARG(((uintptr_t)a.q & 3) == 0 && a.q_stride_b % 2 == 0 && a.q_stride_h % 2 == 0,
-                 "bl_paged_decode: q must be 4-byte aligned with even strides");
-    if (!a.plan_ready) {
-      rc = bl_paged_decode_plan(args, stream);
-      if (rc) return rc;
-    }
-    const WsLayout w = ws_layout(a.batch, a.num_q_heads, a.kv.head_dim, a.kv.block_size, a.max_seq_len);
-    if (!a.workspace || a.workspace_bytes < w.total) {
-      set_error("bl_paged_decode: workspace too small (%zu < %zu bytes)", a.workspace_bytes, w.total);
-      return BL_ERR_CAPACITY;
-    }
-    if (a.kv.dtype == BL_BF16) return launch_tc<__nv_bfloat16>(a, w, s);
-    return launch_tc<__half>(a, w, s);
+  if (is_tc(a)) {
+    WsLayout w;
+    rc = check_tc(a, w);
+    if (rc) return rc;
+    if (a.kv.dtype == BL_BF16) return launch_tc_attention<__nv_bfloat16>(a, w, s);
+    return launch_tc_attention<__half>(a, w, s);
   }
   switch (a.kv.dtype) {
     case BL_F32: return launch_simt<float>(a, s);
     case BL_F16: return launch_simt<__half>(a, s);
     default: return launch_simt<__nv_bfloat16>(a, s);
   }
+}
+
+extern "C" int bl_paged_decode_reduce(const bl_decode_args* args, void* stream) {
+  int rc = check_decode(args, "bl_paged_decode_reduce");
+  if (rc) return rc;
+  const bl_decode_args& a = *args;
+  if (!is_tc(a)) return BL_OK;  // the SIMT path never splits
+  WsLayout w;
+  rc = check_tc(a, w);
+  if (rc) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (a.kv.dtype == BL_BF16) return launch_tc_reduce<__nv_bfloat16>(a, w, s);
+  return launch_tc_reduce<__half>(a, w, s);
+}
+
+extern "C" int bl_paged_decode(const bl_decode_args* args, void* stream) {
+  int rc = check_decode(args, "bl_paged_decode");
+  if (rc) return rc;
+  if (is_tc(*args) && !args->plan_ready) {
+    rc = bl_paged_decode_plan(args, stream);
+    if (rc) return rc;
+  }
+  rc = bl_paged_decode_attention(args, stream);
+  if (rc) return rc;
+  return bl_paged_decode_reduce(args, stream);
 }

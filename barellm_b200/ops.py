@@ -200,14 +200,20 @@ def decode_workspace_bytes(batch: int, num_q_heads: int, head_dim: int, block_si
 
 
 _WORKSPACES: dict[int, torch.Tensor] = {}
+_PLAN_SERIAL: dict[int, int] = {}
+
+
+def _dev_index(device: torch.device) -> int:
+    return device.index if device.index is not None else torch.cuda.current_device()
 
 
 def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
     """Per-device scratch buffer for split-K decode (grown, never shrunk).
 
     Calls on one device share it, so decode calls must be ordered on a single
-    stream (which the engine guarantees)."""
-    idx = device.index if device.index is not None else torch.cuda.current_device()
+    stream (which the engine guarantees).  Growing it invalidates any plan it
+    held."""
+    idx = _dev_index(device)
     ws = _WORKSPACES.get(idx)
     if ws is None or ws.numel() < nbytes:
         size = max(nbytes, 1 << 20)
@@ -215,7 +221,13 @@ def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
             size = max(size, 2 * ws.numel())
         ws = torch.empty(size, dtype=torch.uint8, device=torch.device("cuda", idx))
         _WORKSPACES[idx] = ws
+        _PLAN_SERIAL[idx] = _PLAN_SERIAL.get(idx, 0) + 1
     return ws
+
+
+def plan_serial(device: torch.device) -> int:
+    """Changes whenever the shared workspace's plan is replaced."""
+    return _PLAN_SERIAL.get(_dev_index(device), 0)
 
 
 def _decode_args(
@@ -292,6 +304,9 @@ def paged_decode_plan(
     a, _, ws = _decode_args(q_dummy, key_cache, value_cache, 0, block_tables, seq_lens, max_seq_len, None,
                             q_dummy, row_ids, ws, False, err)
     _raise_rc(nat.load().bl_paged_decode_plan(a, _stream(key_cache.device)))
+    idx = _dev_index(key_cache.device)
+    if _WORKSPACES.get(idx) is ws:
+        _PLAN_SERIAL[idx] = _PLAN_SERIAL.get(idx, 0) + 1
     return ws
 
 
@@ -310,17 +325,29 @@ def paged_decode(
     ws: torch.Tensor | None = None,
     plan_ready: bool = False,
     err: torch.Tensor | None = None,
+    stage: str = "all",
 ) -> torch.Tensor:
     """One-token GQA attention over paged K/V, read in place; returns ``[B, Hq, D]``.
+
+    ``stage``: "all" (plan unless ``plan_ready``, attention, reduce),
+    "attention" (attention kernel only; needs ``plan_ready``) or "reduce"
+    (split-K merge only).
 
     Equals the reference decode chain read -> _pad -> repeat_interleave ->
     attention_mask -> SDPA (src/barellm/attention/backend.py:34-61).
     ``seq_lens`` are post-append lengths (>= 1), ``max_seq_len`` a host-side
     upper bound used only to size the split-K workspace.
     """
-    a, out, _ = _decode_args(q, key_cache, value_cache, layer, block_tables, seq_lens, max_seq_len, scale,
-                             out, row_ids, ws, plan_ready, err)
-    _raise_rc(nat.load().bl_paged_decode(a, _stream(key_cache.device)))
+    a, out, used_ws = _decode_args(q, key_cache, value_cache, layer, block_tables, seq_lens, max_seq_len, scale,
+                                   out, row_ids, ws, plan_ready, err)
+    lib = nat.load()
+    fn = {"all": lib.bl_paged_decode, "attention": lib.bl_paged_decode_attention,
+          "reduce": lib.bl_paged_decode_reduce}[stage]
+    _raise_rc(fn(a, _stream(key_cache.device)))
+    if not plan_ready and stage == "all":
+        idx = _dev_index(key_cache.device)
+        if _WORKSPACES.get(idx) is used_ws:  # this call replaced the shared plan
+            _PLAN_SERIAL[idx] = _PLAN_SERIAL.get(idx, 0) + 1
     return out
 
 

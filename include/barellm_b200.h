@@ -174,8 +174,16 @@ BL_API size_t bl_paged_decode_workspace_bytes(int64_t batch, int64_t num_q_heads
  * depends only on seq_lens, so one plan serves every layer of a step. */
 BL_API int bl_paged_decode_plan(const bl_decode_args* args, void* stream);
 
-/* Runs the plan (built first unless plan_ready), the attention kernel and
- * the split-K reduce kernel. */
+/* The attention kernel alone (the plan must already be in the workspace
+ * on the tensor-core path).  Rows that fit in one chunk get their output
+ * here; longer rows leave (o, lse) partials in the workspace. */
+BL_API int bl_paged_decode_attention(const bl_decode_args* args, void* stream);
+
+/* The split-K reduce alone: merges the partials of multi-chunk rows into
+ * `out`.  A no-op on the SIMT path, which never splits. */
+BL_API int bl_paged_decode_reduce(const bl_decode_args* args, void* stream);
+
+/* All of it: plan (unless plan_ready), attention, reduce. */
 BL_API int bl_paged_decode(const bl_decode_args* args, void* stream);
 
 /* ------------------------------------------------------------------------ */

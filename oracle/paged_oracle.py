@@ -168,3 +168,46 @@ def decode_attention_rows(q, k_rows, v_rows, scale=None):
         p /= p.sum(axis=-1, keepdims=True)
         out[b] = np.einsum("hgt,htd->hgd", p, vb).reshape(q.shape[1], -1)
     return out
+
+
+# ---------------------------------------------------------------------------
+# Timed CPU baseline (bench.py's cpu_baseline leg and --impl reference arm)
+# ---------------------------------------------------------------------------
+def _sdpa_f32(q, k, v, attn_mask):
+    """float32 SDPA with a bool padding mask, as the reference runs on a CPU."""
+    d = q.shape[-1]
+    logits = np.einsum("bhqd,bhkd->bhqk", q, k, optimize=True) * np.float32(1.0 / np.sqrt(d))
+    logits = np.where(attn_mask, logits, np.float32(-np.inf))
+    logits -= logits.max(axis=-1, keepdims=True)
+    p = np.exp(logits, dtype=np.float32)
+    p /= p.sum(axis=-1, keepdims=True)
+    return np.einsum("bhqk,bhkd->bhqd", p, v, optimize=True)
+
+
+def decode_step_cpu(key_cache, value_cache, layer, block_tables, starts, q, k_new, v_new, executor=None,
+                    rows_per_task: int = 1):
+    """One batched decode step exactly as the reference runs it on a CPU, in
+    float32: per-row append (paged_kv_cache.py:151-193), dense read + zero pad
+    (batched_kv_cache.py:65-95), repeat_interleave (backend.py:47-48), padding
+    mask (batched_kv_cache.py:97-102) and SDPA (backend.py:55-61).
+
+    Rows are split into independent groups that run on ``executor``'s threads
+    (each group pads to its own longest row, which changes no result).
+    Returns ``[B, Hq, 1, D]`` float32."""
+    b = q.shape[0]
+    for r in range(b):
+        append_only(key_cache, value_cache, layer, block_tables[r], int(starts[r]), k_new[r : r + 1], v_new[r : r + 1])
+    lens = [int(s) + k_new.shape[2] for s in starts]
+    group = q.shape[1] // key_cache.shape[2]
+
+    def run(lo: int, hi: int):
+        k, v = batch_read_pad(key_cache, value_cache, layer, block_tables[lo:hi], lens[lo:hi])
+        mask = attention_mask(lens[lo:hi], q.shape[2])
+        return lo, _sdpa_f32(q[lo:hi], repeat_kv(k, group), repeat_kv(v, group), mask)
+
+    spans = [(i, min(i + rows_per_task, b)) for i in range(0, b, rows_per_task)]
+    out = np.empty(q.shape, dtype=np.float32)
+    results = executor.map(lambda s: run(*s), spans) if executor is not None else (run(*s) for s in spans)
+    for lo, o in results:
+        out[lo : lo + o.shape[0]] = o
+    return out
