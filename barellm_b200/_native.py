@@ -72,6 +72,9 @@ class AppendArgs(Structure):
         ("new_stride_b", c_int64),
         ("new_stride_h", c_int64),
         ("new_stride_t", c_int64),
+        ("v_stride_b", c_int64),
+        ("v_stride_h", c_int64),
+        ("v_stride_t", c_int64),
         ("start_pos", c_void_p),
         ("new_offsets", c_void_p),
         ("batch", c_int64),

@@ -29,7 +29,8 @@ struct AppendKernelArgs {
   const char* k_new;
   const char* v_new;
   int64_t num_blocks, hkv, bs, row_bytes, layer;
-  int64_t nsb, nsh, nst;  // strides of the new tokens, in bytes
+  int64_t nsb, nsh, nst;  // strides of the new K tokens, in bytes
+  int64_t vsb, vsh, vst;  // strides of the new V tokens, in bytes
   const int32_t* block_tables;
   int64_t bt_stride, bt_width;
   const int32_t* row_ids;
@@ -76,9 +77,10 @@ __global__ void __launch_bounds__(256) paged_append_kernel(const AppendKernelArg
     return;
   }
   const int64_t src = b * a.nsb + (o_b + t) * a.nst + h * a.nsh + (int64_t)v * VEC;
+  const int64_t vsrc = b * a.vsb + (o_b + t) * a.vst + h * a.vsh + (int64_t)v * VEC;
   const int64_t dst = (((a.layer * a.num_blocks + phys) * a.hkv + h) * a.bs + off) * a.row_bytes + (int64_t)v * VEC;
   const V kv = *reinterpret_cast<const V*>(a.k_new + src);
-  const V vv = *reinterpret_cast<const V*>(a.v_new + src);
+  const V vv = *reinterpret_cast<const V*>(a.v_new + vsrc);
   *reinterpret_cast<V*>(a.k_pool + dst) = kv;
   *reinterpret_cast<V*>(a.v_pool + dst) = vv;
 }
@@ -169,7 +171,8 @@ extern "C" int bl_paged_append(const bl_append_args* args, void* stream) {
   const int vec = pick_vec({(uint64_t)row_bytes, (uint64_t)a.kv.k_pool, (uint64_t)a.kv.v_pool,
                             (uint64_t)a.k_new, (uint64_t)a.v_new,
                             (uint64_t)(a.new_stride_b * es), (uint64_t)(a.new_stride_h * es),
-                            (uint64_t)(a.new_stride_t * es)});
+                            (uint64_t)(a.new_stride_t * es), (uint64_t)(a.v_stride_b * es),
+                            (uint64_t)(a.v_stride_h * es), (uint64_t)(a.v_stride_t * es)});
   BL_CHECK_ARG(vec > 0, "bl_paged_append: tensors must be at least 2-byte aligned");
 
   AppendKernelArgs k;
@@ -185,6 +188,9 @@ extern "C" int bl_paged_append(const bl_append_args* args, void* stream) {
   k.nsb = a.new_stride_b * es;
   k.nsh = a.new_stride_h * es;
   k.nst = a.new_stride_t * es;
+  k.vsb = a.v_stride_b * es;
+  k.vsh = a.v_stride_h * es;
+  k.vst = a.v_stride_t * es;
   k.block_tables = a.kv.block_tables;
   k.bt_stride = a.kv.bt_stride;
   k.bt_width = a.kv.bt_width;

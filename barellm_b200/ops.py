@@ -116,14 +116,13 @@ def paged_append(
     pl = _paged_layer(key_cache, value_cache, layer, block_tables, row_ids)
     _check(key.ndim == 4 and value.ndim == 4, "K/V must have shape [B, H, T, D]")
     _check(key.shape == value.shape, "K/V must have identical shape")
-    _check(key.stride() == value.stride(), "K/V must have identical strides")
     _check(key.shape[1] == key_cache.shape[2], "KV-head count cannot change")
     _check(key.shape[2] > 0, "K/V sequence length must be greater than zero")
     _check(key.shape[3] == key_cache.shape[4], "Head dimension cannot change")
     _check(key.dtype == key_cache.dtype, "K/V dtype cannot change")
     _check(key.device == key_cache.device, "K/V device cannot change")
     _check(key.dtype == value.dtype, "K/V dtype must match")
-    _check(key.stride(3) == 1, "K/V head_dim must be contiguous")
+    _check(key.stride(3) == 1 and value.stride(3) == 1, "K/V head_dim must be contiguous")
     _int32_on(start_pos, key.device, "start_pos")
     batch = start_pos.shape[0]
     if new_offsets is None:
@@ -142,6 +141,9 @@ def paged_append(
     a.new_stride_b = key.stride(0) if new_offsets is None else 0
     a.new_stride_h = key.stride(1)
     a.new_stride_t = key.stride(2)
+    a.v_stride_b = value.stride(0) if new_offsets is None else 0
+    a.v_stride_h = value.stride(1)
+    a.v_stride_t = value.stride(2)
     a.start_pos = start_pos.data_ptr()
     a.new_offsets = _ptr(new_offsets)
     a.batch = batch

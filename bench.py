@@ -433,12 +433,13 @@ def run_ours(args, wl_name: str) -> None:
         with torch.cuda.graph(graph, stream=stream):
             work.step()
     torch.cuda.current_stream(device).wait_stream(stream)
-    for _ in range(warmup):
-        graph.replay()
-    torch.cuda.synchronize(device)
     sampler = ClockSampler(local)
     barrier(world, device)
     with sampler:
+        # warm-up right before the timed region, so the GPU never idles
+        # (and drops its clocks) between the two
+        for _ in range(warmup):
+            graph.replay()
         ms = time_steps(graph.replay, steps, device)
     barrier(world, device)
     if int(work.err.item()):

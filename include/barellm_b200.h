@@ -93,7 +93,8 @@ typedef struct bl_paged_layer {
 /*                                                                          */
 /* Token t (0-based) of request b, head h, lives at                         */
 /*   k_new + b*new_stride_b + (o_b + t)*new_stride_t + h*new_stride_h       */
-/* where o_b = new_offsets[b] (ragged, packed along the token axis) or 0.   */
+/* (v_new likewise with the v_stride_* values), where o_b = new_offsets[b]  */
+/* (ragged, packed along the token axis) or 0.                              */
 /* Row b appends n_b tokens: new_offsets[b+1]-new_offsets[b], or            */
 /* max_new_tokens when new_offsets is NULL.  They go to logical positions   */
 /* start_pos[b] .. start_pos[b]+n_b-1.  The last axis (head_dim) must be    */
@@ -105,6 +106,9 @@ typedef struct bl_append_args {
   int64_t new_stride_b;
   int64_t new_stride_h;
   int64_t new_stride_t;
+  int64_t v_stride_b;
+  int64_t v_stride_h;
+  int64_t v_stride_t;
   const int32_t* start_pos;   /* [batch], device */
   const int32_t* new_offsets; /* [batch+1], device, or NULL */
   int64_t batch;
