@@ -38,6 +38,7 @@ EXPORTED = (
     "bl_paged_decode",
     "bl_paged_decode_attention",
     "bl_paged_decode_reduce",
+    "bl_paged_decode_noalloc",
     "bl_paged_prefill",
     "bl_last_error",
     "bl_abi_version",
@@ -174,6 +175,8 @@ def load() -> ctypes.CDLL:
     for fn in (lib.bl_paged_decode, lib.bl_paged_decode_attention, lib.bl_paged_decode_reduce):
         fn.argtypes = [POINTER(DecodeArgs), c_void_p]
         fn.restype = c_int
+    lib.bl_paged_decode_noalloc.argtypes = [POINTER(DecodeArgs), c_void_p]
+    lib.bl_paged_decode_noalloc.restype = c_int
     lib.bl_paged_prefill.argtypes = [POINTER(PrefillArgs), c_void_p]
     lib.bl_paged_prefill.restype = c_int
     lib.bl_last_error.argtypes = []

@@ -867,3 +867,70 @@ extern "C" int bl_paged_decode(const bl_decode_args* args, void* stream) {
   if (rc) return rc;
   return bl_paged_decode_reduce(args, stream);
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free decode
+// ---------------------------------------------------------------------------
+// Some callers cannot hand this library a workspace: a host framework that
+// owns every byte of device memory and passes plugins nothing but input and
+// output pointers, or a latency-critical loop that must never enter
+// cudaMalloc (which can synchronise the whole device).  For them,
+// bl_paged_decode_noalloc runs the same split-K decode with its scratch in
+// the fixed array below instead of a caller workspace.  The array is part of
+// the library image: every GPU that loads the library keeps these 16 MiB for
+// the life of the process.
+namespace bl {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch on the current device.  In host code the
+// symbol is only a stand-in, so the address is looked up once per device (the
+// first call on that device does it, with that device current) and cached.
+void* noalloc_scratch_on_current_device() {
+  static std::mutex mu;
+  static void* ptrs[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    set_error("bl_paged_decode_noalloc: cannot query the current device");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      set_error("bl_paged_decode_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+      return nullptr;
+    }
+    ptrs[dev] = p;
+  }
+  return ptrs[dev];
+}
+
+}  // namespace
+}  // namespace bl
+
+extern "C" int bl_paged_decode_noalloc(const bl_decode_args* args, void* stream) {
+  int rc = check_decode(args, "bl_paged_decode_noalloc");
+  if (rc) return rc;
+  bl_decode_args a = *args;
+  if (is_tc(a)) {
+    const WsLayout w = ws_layout(a.batch, a.num_q_heads, a.kv.head_dim, a.kv.block_size, a.max_seq_len);
+    if (w.total > kNoAllocScratchBytes) {
+      set_error("bl_paged_decode_noalloc: this batch needs %zu bytes of split-K scratch but the built-in scratch "
+                "holds %zu; use bl_paged_decode with a caller workspace", w.total, kNoAllocScratchBytes);
+      return BL_ERR_CAPACITY;
+    }
+    void* scratch = noalloc_scratch_on_current_device();
+    if (!scratch) return BL_ERR_LAUNCH;
+    a.workspace = scratch;
+    a.workspace_bytes = kNoAllocScratchBytes;
+  }
+  // The plan is always rebuilt: the scratch holds whatever the previous call
+  // left there.  Nothing in it has to start at zero -- the plan kernel writes
+  // every entry the attention and reduce kernels read.
+  a.plan_ready = 0;
+  return bl_paged_decode(&a, stream);
+}

@@ -353,6 +353,48 @@ def paged_decode(
     return out
 
 
+def paged_decode_noalloc(
+    q: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    layer: int,
+    block_tables: torch.Tensor,
+    seq_lens: torch.Tensor,
+    max_seq_len: int,
+    out: torch.Tensor,
+    *,
+    scale: float | None = None,
+    row_ids: torch.Tensor | None = None,
+    err: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Decode through ``bl_paged_decode_noalloc``: the split-K scratch is the
+    library's built-in 16 MiB array, so neither this call nor the library
+    allocates device memory (the caller passes ``out``).  For callers whose
+    host framework owns all device memory or who must keep cudaMalloc off the
+    decode loop.  Calls share the one array: order them on one stream."""
+    pl = _paged_layer(key_cache, value_cache, layer, block_tables, row_ids)
+    _require_cuda(q, "q")
+    q3 = q[:, :, 0, :] if q.ndim == 4 else q
+    out3 = out[:, :, 0, :] if out.ndim == 4 else out
+    _check(q3.ndim == 3 and q3.stride(2) == 1, "q must be [B, Hq, D] or [B, Hq, 1, D], D contiguous")
+    _check(q3.dtype == key_cache.dtype and q3.device == key_cache.device, "q must match the K/V pool dtype and device")
+    _check(out3.shape == q3.shape and out3.stride(2) == 1 and out3.dtype == q3.dtype, "out must match q")
+    _int32_on(seq_lens, q3.device, "seq_lens")
+    a = nat.DecodeArgs()
+    a.kv = pl
+    a.q = q3.data_ptr()
+    a.q_stride_b, a.q_stride_h = q3.stride(0), q3.stride(1)
+    a.out = out3.data_ptr()
+    a.out_stride_b, a.out_stride_h = out3.stride(0), out3.stride(1)
+    a.seq_lens = seq_lens.data_ptr()
+    a.batch, a.num_q_heads = q3.shape[0], q3.shape[1]
+    a.scale = 1.0 / math.sqrt(q3.shape[2]) if scale is None else float(scale)
+    a.max_seq_len = max_seq_len
+    a.err = _ptr(err)
+    _raise_rc(nat.load().bl_paged_decode_noalloc(a, _stream(q3.device)))
+    return out
+
+
 def paged_prefill(
     q: torch.Tensor,
     key_cache: torch.Tensor,

@@ -190,6 +190,22 @@ BL_API int bl_paged_decode_reduce(const bl_decode_args* args, void* stream);
 /* All of it: plan (unless plan_ready), attention, reduce. */
 BL_API int bl_paged_decode(const bl_decode_args* args, void* stream);
 
+/* Allocation-free variant of bl_paged_decode.  No counterpart in the
+ * reference: it exists for callers that cannot provide device scratch -- a
+ * host framework that owns all device memory and hands a plugin only its
+ * input and output pointers, or a hot loop that must never call cudaMalloc.
+ * The split-K scratch lives in a fixed 16 MiB array inside the library,
+ * which every GPU that loads the
+ * library keeps until the process exits; `workspace`, `workspace_bytes` and
+ * `plan_ready` are ignored and no memory is allocated.  A batch whose split-K
+ * scratch (bl_paged_decode_workspace_bytes) exceeds 16 MiB is rejected with
+ * BL_ERR_CAPACITY.  The first call on a device looks up the array's device
+ * address with that device current; make that first call before any stream
+ * capture.  All calls share the one array: calls that overlap on the GPU (two
+ * streams, or two host threads) race and corrupt each other's results, so
+ * order them on one stream. */
+BL_API int bl_paged_decode_noalloc(const bl_decode_args* args, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Prefill attention: causal attention of new query tokens over a paged      */
 /* prefix plus themselves, read in place.                                    */
