@@ -48,15 +48,19 @@ WORKLOADS = {
     # across the GPUs, lengths log-uniform 1k..32k, ~150 GB KV pool per GPU
     "decode_qwen8b_long": dict(hq=32, hkv=8, d=128, bs=16, batch=256, len_lo=1024, len_hi=32768, log_uniform=True,
                                pool_bytes=150e9, shard_batch=True, scale=1.0),
+    # paged chunked prefill at Qwen3-8B attention shapes: 32 requests, each a
+    # paged prefix of U{0..8192} tokens plus a new chunk of U{512..2048}
+    "prefill_qwen8b": dict(kind="prefill", hq=32, hkv=8, d=128, bs=16, batch=32, prefix_lo=0, prefix_hi=8192,
+                           chunk_lo=512, chunk_hi=2048, pool_blocks=65536, shard_batch=True),
 }
-PEAKS_FALLBACK = {"hbm_gbs": 6650.0}
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 
 
-def load_peaks() -> tuple[float, str]:
+def load_peaks(key: str = "hbm_gbs") -> tuple[float, str]:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
-        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
-    return PEAKS_FALLBACK["hbm_gbs"], "fallback"
+        return float(json.loads(p.read_text())[key]), "measured"
+    return PEAKS_FALLBACK[key], "fallback"
 
 
 # ---------------------------------------------------------------------------
@@ -382,6 +386,16 @@ def cpu_sample_state(wl: dict, lens: list[int], seed: int = 5):
     return kc, vc, tables, np.array(lens), q, kn, vn
 
 
+def cpu_sample_lens(lens: list[int], max_rows: int, max_tokens: int) -> list[int]:
+    """The first rows of the workload, up to max_rows rows / max_tokens tokens (>= 1 row)."""
+    out: list[int] = []
+    for n in lens[:max_rows]:
+        if out and sum(out) + n > max_tokens:
+            break
+        out.append(n)
+    return out
+
+
 def cpu_bytes(wl: dict, lens) -> int:
     """Same algorithmic byte count as the GPU arm (bf16 elements)."""
     return sum(n + 1 for n in lens) * wl["hkv"] * wl["d"] * 2 * 2 + 2 * len(lens) * wl["hq"] * wl["d"] * 2
@@ -470,7 +484,7 @@ def run_ours(args, wl_name: str) -> None:
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        lens = work_lens[: min(8, work.batch)]
+        lens = cpu_sample_lens(work_lens, 8, 20000)
         gbs, runs, per = cpu_run(wl, lens, seconds=args.cpu_seconds, min_runs=1, threads=threads)
         cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port",
                "sample": f"{len(lens)} of {work.batch} requests ({sum(lens)} cached tokens), "
@@ -542,7 +556,7 @@ def run_reference(args, wl_name: str) -> None:
     threads = os.cpu_count() or 1
     # size the per-step sample so the whole run stays within ~2 minutes
     budget = 120.0 / max(args.steps + args.warmup, 1)
-    cand = all_lens[: min(8, len(all_lens))]
+    cand = cpu_sample_lens(all_lens, 8, 20000)
     _, _, per_row = cpu_run(wl, cand[:1], seconds=0.0, min_runs=1, threads=threads)
     n_rows = int(max(1, min(len(cand), budget / max(per_row, 1e-6))))
     lens = cand[:n_rows]
@@ -582,6 +596,282 @@ def run_reference(args, wl_name: str) -> None:
     print(json.dumps(res), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# chunked prefill
+# ---------------------------------------------------------------------------
+def prefill_lengths(wl: dict, seed: int) -> tuple[np.ndarray, np.ndarray]:
+    rs = np.random.RandomState(seed)
+    prefix = rs.randint(wl["prefix_lo"], wl["prefix_hi"] + 1, size=wl["batch"]).astype(np.int64)
+    chunk = rs.randint(wl["chunk_lo"], wl["chunk_hi"] + 1, size=wl["batch"]).astype(np.int64)
+    return prefix, chunk
+
+
+def prefill_flops(hq: int, d: int, prefix, chunk) -> float:
+    """4 * Hq * D * (C*P + C(C+1)/2) per request: Q.K^T and P.V over the causal keys."""
+    return float(sum(4 * hq * d * (c * p + c * (c + 1) / 2) for p, c in zip(prefix, chunk)))
+
+
+class PrefillWorkload:
+    """One GPU's share of the chunked-prefill workload, device resident."""
+
+    def __init__(self, wl: dict, rank: int, world: int, device: torch.device, seed: int = 4321):
+        from barellm_b200 import ops
+
+        self.wl = wl
+        self.device = device
+        prefix_all, chunk_all = prefill_lengths(wl, seed)
+        mine = place_requests(prefix_all + chunk_all, world)[rank]
+        self.prefix = [int(prefix_all[i]) for i in mine]
+        self.chunk = [int(chunk_all[i]) for i in mine]
+        b = len(mine)
+        self.batch = b
+        hq, hkv, d, bs = wl["hq"], wl["hkv"], wl["d"], wl["bs"]
+        self.pool_blocks = wl["pool_blocks"]
+        rs = np.random.RandomState(seed + rank)
+        free = list(rs.permutation(self.pool_blocks))
+        totals = [p + c for p, c in zip(self.prefix, self.chunk)]
+        tables = [[int(free.pop()) for _ in range(-(-n // bs))] for n in totals]
+        bt = np.full((b, max(len(t) for t in tables)), -1, dtype=np.int32)
+        for i, t in enumerate(tables):
+            bt[i, : len(t)] = t
+        self.bt = torch.from_numpy(bt).to(device)
+        shape = (1, self.pool_blocks, hkv, bs, d)
+        self.k_cache = torch.empty(shape, dtype=torch.bfloat16, device=device)
+        self.v_cache = torch.empty(shape, dtype=torch.bfloat16, device=device)
+        gen = torch.Generator(device=device)
+        gen.manual_seed(seed + rank)
+        zeros = torch.zeros(b, dtype=torch.int32, device=device)
+        if sum(self.prefix):
+            n = sum(self.prefix)
+            kh = torch.randn((1, hkv, n, d), generator=gen, device=device).to(torch.bfloat16)
+            vh = torch.randn((1, hkv, n, d), generator=gen, device=device).to(torch.bfloat16)
+            offs = torch.tensor(np.concatenate([[0], np.cumsum(self.prefix)]), dtype=torch.int32, device=device)
+            ops.paged_append(self.k_cache, self.v_cache, 0, self.bt, zeros, kh, vh, new_offsets=offs,
+                             max_new_tokens=max(max(self.prefix), 1))
+            del kh, vh
+        nc = sum(self.chunk)
+        # q as the model produces it: [1, T, Hq, D] memory viewed as [1, Hq, T, D]
+        self.q = torch.randn((1, nc, hq, d), generator=gen, device=device).to(torch.bfloat16).transpose(1, 2)
+        self.k_new = torch.randn((1, nc, hkv, d), generator=gen, device=device).to(torch.bfloat16).transpose(1, 2)
+        self.v_new = torch.randn((1, nc, hkv, d), generator=gen, device=device).to(torch.bfloat16).transpose(1, 2)
+        self.q_offs = torch.tensor(np.concatenate([[0], np.cumsum(self.chunk)]), dtype=torch.int32, device=device)
+        self.starts = torch.tensor(self.prefix, dtype=torch.int32, device=device)
+        self.seq_lens = torch.tensor(totals, dtype=torch.int32, device=device)
+        self.out = torch.empty((1, nc, hq, d), dtype=torch.bfloat16, device=device).transpose(1, 2)
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        self.flops = prefill_flops(hq, d, self.prefix, self.chunk)
+        torch.cuda.synchronize(device)
+
+    def append(self) -> None:
+        from barellm_b200 import ops
+
+        ops.paged_append(self.k_cache, self.v_cache, 0, self.bt, self.starts, self.k_new, self.v_new,
+                         new_offsets=self.q_offs, max_new_tokens=max(self.chunk), err=self.err)
+
+    def attention(self) -> None:
+        from barellm_b200 import ops
+
+        ops.paged_prefill(self.q, self.k_cache, self.v_cache, 0, self.bt, self.seq_lens, q_offsets=self.q_offs,
+                          max_q_len=max(self.chunk), out=self.out, err=self.err)
+
+    def step(self) -> None:
+        self.append()
+        self.attention()
+
+
+def prefill_e2e(wl: dict, work: PrefillWorkload, steps: int, warmup: int, device) -> dict:
+    """Chunked prefill through the public API, one request at a time as the
+    engine's prefill does: pinned host chunk -> PagedLayerKV attend -> host."""
+    from barellm_b200 import BlockPool, CudaPagedAttentionBackend, KVCacheManager, PagedKVCache, ops
+
+    hq, hkv, d, bs = wl["hq"], wl["hkv"], wl["d"], wl["bs"]
+    totals = [p + c for p, c in zip(work.prefix, work.chunk)]
+    need = sum(-(-n // bs) for n in totals)
+    kv = PagedKVCache(1, need + 64, hkv, bs, d, dtype=torch.bfloat16, device=device, max_requests=work.batch)
+    pool = BlockPool(need + 64)
+    pool.free_ids = [int(x) for x in np.random.RandomState(7).permutation(need + 64)]
+    mgr = KVCacheManager(bs, pool, kv)
+
+    class Req:
+        def __init__(self, i, n):
+            self.id, self.seq_len = f"p{i}", n
+
+    layers = []
+    for i, (p, n) in enumerate(zip(work.prefix, totals)):
+        r = Req(i, n)
+        assert mgr.allocate_request(r)
+        layer = mgr.get_cache(r).layer(0)
+        if p:
+            kd, vd = ops.paged_gather(work.k_cache, work.v_cache, 0, work.bt[i : i + 1],
+                                      torch.tensor([p], dtype=torch.int32, device=device), p)
+            layer.append_only(kd, vd)
+        layers.append(layer)
+    offs = [0] + list(np.cumsum(work.chunk))
+    host = [(work.q[:, :, offs[i] : offs[i + 1]].transpose(1, 2).contiguous().cpu().pin_memory(),
+             work.k_new[:, :, offs[i] : offs[i + 1]].transpose(1, 2).contiguous().cpu().pin_memory(),
+             work.v_new[:, :, offs[i] : offs[i + 1]].transpose(1, 2).contiguous().cpu().pin_memory())
+            for i in range(work.batch)]
+    dev = [(torch.empty_like(q, device=device), torch.empty_like(k, device=device), torch.empty_like(v, device=device))
+           for q, k, v in host]
+    outs_h = [torch.empty((1, c, hq, d), dtype=torch.bfloat16).pin_memory() for c in work.chunk]
+    backend = CudaPagedAttentionBackend()
+
+    def one():
+        for i, layer in enumerate(layers):
+            layer._request.layer_seq_lens[0] = work.prefix[i]  # re-prefill the same chunk each step
+            qd, kd, vd = dev[i]
+            qd.copy_(host[i][0], non_blocking=True)
+            kd.copy_(host[i][1], non_blocking=True)
+            vd.copy_(host[i][2], non_blocking=True)
+            out = backend.attend(qd.transpose(1, 2), kd.transpose(1, 2), vd.transpose(1, 2), layer, hq // hkv)
+            outs_h[i].copy_(out.transpose(1, 2), non_blocking=True)
+
+    for _ in range(warmup):
+        one()
+    torch.cuda.synchronize(device)
+    ms = time_steps(one, steps, device)
+    kv.check_device_errors()
+    h2d = sum((q.numel() + k.numel() + v.numel()) * 2 for q, k, v in host)
+    return {"ms": ms, "h2d": h2d, "d2h": sum(o.numel() * 2 for o in outs_h)}
+
+
+def run_prefill(args, wl_name: str) -> None:
+    rank, world, local = dist_env()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    wl = WORKLOADS[wl_name]
+    work = PrefillWorkload(wl, rank, world, device)
+    steps, warmup = args.steps, args.warmup
+    work.step()
+    torch.cuda.synchronize(device)
+    sampler = ClockSampler(local)
+    barrier(world, device)
+    with sampler:
+        for _ in range(warmup):
+            work.step()
+        ms = time_steps(work.step, steps, device)
+    barrier(world, device)
+    if int(work.err.item()):
+        raise RuntimeError(f"device error word {int(work.err.item())}")
+    ms_max = allreduce(ms, "max", world, device)
+    flops_all = allreduce(work.flops, "sum", world, device)
+    value = flops_all * steps / (ms_max / 1e3) / 1e12
+    att_ms = time_steps(work.attention, max(steps, 5), device) / max(steps, 5)
+    peak, peak_src = load_peaks("bf16_tflops")
+    achieved = work.flops / (att_ms / 1e3) / 1e12
+    e2e = prefill_e2e(wl, work, steps, warmup, device)
+    e2e_ms = allreduce(e2e["ms"], "max", world, device)
+    e2e_value = flops_all * steps / (e2e_ms / 1e3) / 1e12
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = prefill_cpu(wl, work.prefix[0], min(work.chunk[0], 256), args.cpu_seconds)
+    if rank == 0:
+        res = {
+            "metric": "paged chunked-prefill attention TFLOP/s",
+            "value": round(value, 2),
+            "unit": "TFLOP/s",
+            "n_gpus": world,
+            "steps": steps,
+            "warmup": warmup,
+            "ms_per_step": ms_max / steps,
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic",
+            "config": {
+                "workload": wl_name,
+                "model_shapes": f"{wl['hq']}q/{wl['hkv']}kv heads, head_dim {wl['d']}, block_size {wl['bs']}",
+                "requests_total": wl["batch"],
+                "prefix": f"uniform {wl['prefix_lo']}..{wl['prefix_hi']}",
+                "chunk": f"uniform {wl['chunk_lo']}..{wl['chunk_hi']}",
+                "flops_per_step_per_gpu": work.flops,
+                "step": "packed chunk append + paged prefill attention (bottom-right causal)",
+                "parallelism": f"dp{world} by request",
+                "l2": "K/V re-read per query tile; working set > L2",
+            },
+            "roofline": {"kernel": "prefill_tc_kernel", "bound": "tensor", "achieved": round(achieved, 2),
+                         "peak": peak, "peak_source": f"{peak_src} bf16_tflops (cuBLAS burst)", "unit": "TFLOP/s",
+                         "frac": round(achieved / peak, 4), "traffic": None, "launch_ms": att_ms},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": e2e["h2d"],
+                    "d2h_bytes_per_step": e2e["d2h"], "ms_per_step": e2e_ms / steps,
+                    "path": "PagedKVCache + CudaPagedAttentionBackend.attend per request (engine prefill path)"},
+            "gpu_launches": 2 * steps,
+            "clocks": sampler.summary(),
+        }
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def prefill_cpu(wl: dict, prefix: int, chunk: int, seconds: float, runs_min: int = 1, warmup: int = 1) -> dict:
+    """The reference's read + repeat_interleave + masked SDPA for one request
+    (float32 numpy), timed on the host."""
+    from oracle import paged_oracle as orc
+
+    hq, hkv, d, bs = wl["hq"], wl["hkv"], wl["d"], wl["bs"]
+    rs = np.random.RandomState(3)
+    n = prefix + chunk
+    nb = -(-n // bs)
+    kc = np.zeros((1, nb, hkv, bs, d), np.float32)
+    vc = np.zeros_like(kc)
+    table = rs.permutation(nb)
+    orc.append_only(kc, vc, 0, table, 0, rs.standard_normal((1, hkv, n, d)).astype(np.float32),
+                    rs.standard_normal((1, hkv, n, d)).astype(np.float32))
+    q = rs.standard_normal((1, hq, chunk, d)).astype(np.float32)
+    g = hq // hkv
+
+    def run():
+        k, v = orc.read(kc, vc, 0, table, n)
+        mask = orc.causal_mask_bottom_right(chunk, n)[None, None]
+        return orc._sdpa_f32(q, orc.repeat_kv(k, g), orc.repeat_kv(v, g), mask)
+
+    for _ in range(warmup):
+        run()
+    t0 = time.perf_counter()
+    runs = 0
+    while runs < runs_min or time.perf_counter() - t0 < seconds:
+        run()
+        runs += 1
+    el = (time.perf_counter() - t0) / runs
+    fl = prefill_flops(hq, d, [prefix], [chunk])
+    return {"value": round(fl / el / 1e12, 6), "unit": "TFLOP/s", "cores": os.cpu_count() or 1, "kind": "port",
+            "sample": f"one request, prefix {prefix} + chunk {chunk}, {runs} runs of {el:.3f} s, float32 numpy"}
+
+
+def run_reference_prefill(args, wl_name: str) -> None:
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    wl = WORKLOADS[wl_name]
+    prefix, chunk = prefill_lengths(wl, 4321)
+    budget = 120.0 / max(args.steps + args.warmup, 1)
+    c = 256
+    while True:  # shrink the sampled chunk until one step fits the per-step budget
+        probe = prefill_cpu(wl, int(prefix[0]), c, 0.0)
+        per = float(probe["sample"].split(" runs of ")[1].split(" s")[0])
+        if per <= budget or c <= 16:
+            break
+        c //= 2
+    cpu = prefill_cpu(wl, int(prefix[0]), c, 0.0, runs_min=args.steps, warmup=args.warmup)
+    per = float(cpu["sample"].split(" runs of ")[1].split(" s")[0])
+    res = {"metric": "paged chunked-prefill attention TFLOP/s", "value": cpu["value"], "unit": "TFLOP/s",
+           "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": per * 1e3,
+           "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+           "config": {"workload": wl_name}, "impl": "reference", "cpu_baseline": cpu,
+           "e2e": {"value": cpu["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(res), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -594,10 +884,11 @@ def main() -> None:
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    prefill = WORKLOADS[args.workload].get("kind") == "prefill"
     if args.impl == "reference":
-        run_reference(args, args.workload)
+        (run_reference_prefill if prefill else run_reference)(args, args.workload)
     else:
-        run_ours(args, args.workload)
+        (run_prefill if prefill else run_ours)(args, args.workload)
 
 
 if __name__ == "__main__":
