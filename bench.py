@@ -432,7 +432,7 @@ def run_ours(args, wl_name: str) -> None:
 
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
     wl = WORKLOADS[wl_name]
     work = DecodeWorkload(wl, rank, world, device)
     steps, warmup = args.steps, args.warmup
@@ -744,7 +744,7 @@ def run_prefill(args, wl_name: str) -> None:
 
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
     wl = WORKLOADS[wl_name]
     work = PrefillWorkload(wl, rank, world, device)
     steps, warmup = args.steps, args.warmup
