@@ -1,0 +1,215 @@
+"""The callers of the paged-KV path: a Qwen3 decoder and a batched engine loop.
+
+This is the harness that drives the path end to end (prefill every request,
+then batched greedy decode), the way the reference's Engine does
+(src/barellm/engine/engine.py:187-546) over its Qwen3 model
+(src/barellm/models/qwen3.py, block.py, attention.py, rope.py, norm.py,
+mlp.py, embedding.py).  The model math follows the reference exactly --
+pre-norm blocks, QK-RMSNorm before half-split RoPE, GQA attention through an
+``AttentionBackend``, SwiGLU, tied LM head -- so that two runs of the same
+weights differ only in the attention backend and cache.  Weights are random
+(no checkpoint is needed to measure the path).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from .backend import CudaPagedAttentionBackend
+from .batched_kv_cache import BatchKVCache
+from .block_pool import BlockPool
+from .kv_cache_manager import KVCacheManager
+from .paged_kv_cache import PagedKVCache
+
+
+@dataclass(frozen=True)
+class Qwen3Shape:
+    vocab_size: int = 151936
+    hidden_size: int = 1024
+    intermediate_size: int = 3072
+    head_dim: int = 128
+    num_layers: int = 28
+    num_heads: int = 16
+    num_kv_heads: int = 8
+    rope_theta: float = 1_000_000.0
+    rms_norm_eps: float = 1e-6
+
+
+QWEN3_06B = Qwen3Shape()
+
+
+class RMSNorm(nn.Module):
+    """fp32 mean-square normalisation, weight applied in fp32, cast back (norm.py)."""
+
+    def __init__(self, dim: int, eps: float) -> None:
+        super().__init__()
+        self.weight = nn.Parameter(torch.ones(dim))
+        self.eps = eps
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        xf = x.float()
+        xf = xf * torch.rsqrt(xf.pow(2).mean(dim=-1, keepdim=True) + self.eps)
+        return (xf * self.weight).to(x.dtype)
+
+
+def rope_cos_sin(head_dim: int, theta: float, position_ids: torch.Tensor, dtype: torch.dtype):
+    """Half-split RoPE tables [B, 1, T, D] in the activation dtype (rope.py:25-50)."""
+    inv_freq = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float32, device=position_ids.device) / head_dim))
+    angles = position_ids.to(torch.float32)[..., None] * inv_freq
+    angles = torch.cat((angles, angles), dim=-1)
+    return angles.cos().unsqueeze(1).to(dtype), angles.sin().unsqueeze(1).to(dtype)
+
+
+def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    half = x.shape[-1] // 2
+    rot = torch.cat((-x[..., half:], x[..., :half]), dim=-1)
+    return x * cos + rot * sin
+
+
+class Attention(nn.Module):
+    def __init__(self, s: Qwen3Shape, backend) -> None:
+        super().__init__()
+        self.s = s
+        self.q_proj = nn.Linear(s.hidden_size, s.num_heads * s.head_dim, bias=False)
+        self.k_proj = nn.Linear(s.hidden_size, s.num_kv_heads * s.head_dim, bias=False)
+        self.v_proj = nn.Linear(s.hidden_size, s.num_kv_heads * s.head_dim, bias=False)
+        self.o_proj = nn.Linear(s.num_heads * s.head_dim, s.hidden_size, bias=False)
+        self.q_norm = RMSNorm(s.head_dim, s.rms_norm_eps)
+        self.k_norm = RMSNorm(s.head_dim, s.rms_norm_eps)
+        self.backend = backend
+
+    def forward(self, x, cos, sin, layer_cache) -> torch.Tensor:
+        b, t, _ = x.shape
+        s = self.s
+        q = self.q_proj(x).view(b, t, s.num_heads, s.head_dim).transpose(1, 2)
+        k = self.k_proj(x).view(b, t, s.num_kv_heads, s.head_dim).transpose(1, 2)
+        v = self.v_proj(x).view(b, t, s.num_kv_heads, s.head_dim).transpose(1, 2)
+        q = apply_rope(self.q_norm(q), cos, sin)
+        k = apply_rope(self.k_norm(k), cos, sin)
+        ctx = self.backend.attend(q, k, v, layer_cache, s.num_heads // s.num_kv_heads)
+        return self.o_proj(ctx.transpose(1, 2).reshape(b, t, -1))
+
+
+class Block(nn.Module):
+    def __init__(self, s: Qwen3Shape, backend) -> None:
+        super().__init__()
+        self.input_layernorm = RMSNorm(s.hidden_size, s.rms_norm_eps)
+        self.self_attn = Attention(s, backend)
+        self.post_attention_layernorm = RMSNorm(s.hidden_size, s.rms_norm_eps)
+        self.gate_proj = nn.Linear(s.hidden_size, s.intermediate_size, bias=False)
+        self.up_proj = nn.Linear(s.hidden_size, s.intermediate_size, bias=False)
+        self.down_proj = nn.Linear(s.intermediate_size, s.hidden_size, bias=False)
+
+    def forward(self, x, cos, sin, layer_cache) -> torch.Tensor:
+        x = x + self.self_attn(self.input_layernorm(x), cos, sin, layer_cache)
+        h = self.post_attention_layernorm(x)
+        return x + self.down_proj(F.silu(self.gate_proj(h)) * self.up_proj(h))
+
+
+class Qwen3(nn.Module):
+    """Qwen3 decoder with tied embeddings; attention goes through ``backend``."""
+
+    def __init__(self, s: Qwen3Shape = QWEN3_06B, backend=None) -> None:
+        super().__init__()
+        self.s = s
+        self.backend = backend if backend is not None else CudaPagedAttentionBackend()
+        self.embed = nn.Parameter(torch.empty(s.vocab_size, s.hidden_size))
+        nn.init.normal_(self.embed, mean=0.0, std=0.02)
+        self.layers = nn.ModuleList([Block(s, self.backend) for _ in range(s.num_layers)])
+        self.norm = RMSNorm(s.hidden_size, s.rms_norm_eps)
+
+    def set_backend(self, backend) -> None:
+        self.backend = backend
+        for blk in self.layers:
+            blk.self_attn.backend = backend
+
+    def forward(self, token_ids: torch.Tensor, position_ids: torch.Tensor, kv_cache=None) -> torch.Tensor:
+        h = self.embed[token_ids]
+        cos, sin = rope_cos_sin(self.s.head_dim, self.s.rope_theta, position_ids, h.dtype)
+        for i, blk in enumerate(self.layers):
+            h = blk(h, cos, sin, None if kv_cache is None else kv_cache.layer(i))
+        return torch.matmul(self.norm(h), self.embed.T)
+
+
+def random_qwen3(shape: Qwen3Shape = QWEN3_06B, dtype=torch.bfloat16, device="cuda", seed: int = 0) -> Qwen3:
+    torch.manual_seed(seed)
+    with torch.device("cpu"):
+        model = Qwen3(shape)
+    return model.to(device=device, dtype=dtype).eval()
+
+
+class _Request:
+    def __init__(self, rid: str, tokens: list[int]) -> None:
+        self.id = rid
+        self.tokens = list(tokens)
+
+    @property
+    def seq_len(self) -> int:
+        return len(self.tokens)
+
+
+class PagedEngine:
+    """Prefill-then-batched-greedy-decode over a paged cache on one GPU.
+
+    Each request is prefilled on its own (as the reference engine does, through
+    the single-request PagedLayerKV path, engine.py:226-257); every decode step
+    then runs all requests as one BatchKVCache batch (engine.py:458-488)."""
+
+    def __init__(self, model: Qwen3, num_blocks: int, block_size: int = 16, max_requests: int = 256) -> None:
+        s = model.s
+        dev = next(model.parameters()).device
+        dtype = next(model.parameters()).dtype
+        self.model = model
+        self.block_size = block_size
+        self.cache = PagedKVCache(s.num_layers, num_blocks, s.num_kv_heads, block_size, s.head_dim, dtype=dtype,
+                                  device=dev, max_requests=max_requests)
+        self.pool = BlockPool(num_blocks)
+        self.manager = KVCacheManager(block_size, self.pool, self.cache)
+        self.device = dev
+
+    @staticmethod
+    def blocks_needed(prompt_lens: list[int], max_new: int, block_size: int) -> int:
+        return sum(math.ceil((n + max_new) / block_size) for n in prompt_lens)
+
+    @torch.inference_mode()
+    def generate(self, prompts: list[list[int]], max_new_tokens: int, timings: dict | None = None) -> list[list[int]]:
+        reqs = [_Request(f"req-{i}", p) for i, p in enumerate(prompts)]
+        dev = self.device
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t2 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for r in reqs:
+            if not self.manager.allocate_request(r):
+                raise RuntimeError("KV pool exhausted during prefill")
+            ids = torch.tensor([r.tokens], dtype=torch.long, device=dev)
+            pos = torch.arange(r.seq_len, device=dev).unsqueeze(0)
+            logits = self.model(ids, pos, kv_cache=self.manager.get_cache(r))
+            r.tokens.append(int(torch.argmax(logits[0, -1]).item()))
+        t1.record()
+        for _ in range(max_new_tokens - 1):
+            for r in reqs:
+                if not self.manager.allocate_request(r):
+                    raise RuntimeError("KV pool exhausted during decode")
+            ids = torch.tensor([[r.tokens[-1]] for r in reqs], dtype=torch.long, device=dev)
+            pos = torch.tensor([[r.seq_len - 1] for r in reqs], dtype=torch.long, device=dev)
+            logits = self.model(ids, pos, kv_cache=BatchKVCache([self.manager.get_cache(r) for r in reqs]))
+            nxt = torch.argmax(logits[:, -1], dim=-1).tolist()
+            for r, tok in zip(reqs, nxt):
+                r.tokens.append(int(tok))
+        t2.record()
+        torch.cuda.synchronize(dev)
+        self.cache.check_device_errors()
+        if timings is not None:
+            timings["prefill_ms"] = t0.elapsed_time(t1)
+            timings["decode_ms"] = t1.elapsed_time(t2)
+            timings["decode_steps"] = max_new_tokens - 1
+        out = [r.tokens[len(p):] for r, p in zip(reqs, prompts)]
+        for r in reqs:
+            self.manager.free_request(r.id)
+        return out

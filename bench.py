@@ -52,6 +52,10 @@ WORKLOADS = {
     # paged prefix of U{0..8192} tokens plus a new chunk of U{512..2048}
     "prefill_qwen8b": dict(kind="prefill", hq=32, hkv=8, d=128, bs=16, batch=32, prefix_lo=0, prefix_hi=8192,
                            chunk_lo=512, chunk_hi=2048, pool_blocks=65536, shard_batch=True),
+    # end to end: Qwen3-0.6B architecture, random bf16 weights, 128 requests of
+    # random token ids (prompts U{64..2048}) placed across the GPUs, greedy
+    # decoding of 256 new tokens through the paged engine
+    "e2e_qwen06b": dict(kind="e2e", batch=128, prompt_lo=64, prompt_hi=2048, new_tokens=256, shard_batch=True),
 }
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 
@@ -872,6 +876,80 @@ def run_reference_prefill(args, wl_name: str) -> None:
     print(json.dumps(res), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# end to end (model + engine)
+# ---------------------------------------------------------------------------
+def run_e2e(args, wl_name: str) -> None:
+    from barellm_b200.engine import QWEN3_06B, PagedEngine, random_qwen3
+
+    rank, world, local = dist_env()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
+    wl = WORKLOADS[wl_name]
+    rs = np.random.RandomState(2024)
+    lens = rs.randint(wl["prompt_lo"], wl["prompt_hi"] + 1, size=wl["batch"])
+    prompts_all = [list(rs.randint(0, QWEN3_06B.vocab_size, size=int(n))) for n in lens]
+    mine = place_requests(lens, world)[rank]
+    prompts = [prompts_all[i] for i in mine]
+    n_new = wl["new_tokens"]
+    model = random_qwen3(QWEN3_06B, dtype=torch.bfloat16, device=device, seed=0)
+    blocks = PagedEngine.blocks_needed([len(p) for p in prompts], n_new, 16) + 16
+    engine = PagedEngine(model, num_blocks=blocks, max_requests=len(prompts))
+    # warm-up: a short run over the first requests (kernels, allocator, cuBLAS)
+    engine.generate(prompts[: min(4, len(prompts))], max_new_tokens=min(8, n_new))
+    barrier(world, device)
+    sampler = ClockSampler(local)
+    tm: dict = {}
+    with sampler:
+        out = engine.generate(prompts, max_new_tokens=n_new, timings=tm)
+    barrier(world, device)
+    decode_tokens = allreduce(float(len(prompts) * tm["decode_steps"]), "sum", world, device)
+    decode_ms = allreduce(tm["decode_ms"], "max", world, device)
+    prefill_ms = allreduce(tm["prefill_ms"], "max", world, device)
+    prompt_tokens = allreduce(float(sum(len(p) for p in prompts)), "sum", world, device)
+    value = decode_tokens / (decode_ms / 1e3)
+    s = QWEN3_06B
+    mid = [len(p) + n_new // 2 for p in prompts]
+    kv_mid = sum(mid) * s.num_layers * s.num_kv_heads * s.head_dim * 2 * 2
+    if rank == 0:
+        res = {
+            "metric": "decode tok/s",
+            "value": round(value, 1),
+            "unit": "tok/s",
+            "n_gpus": world,
+            "steps": tm["decode_steps"],
+            "warmup": 1,
+            "ms_per_step": decode_ms / tm["decode_steps"],
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (random token ids, random-init weights)",
+            "config": {"workload": wl_name, "model": "Qwen3-0.6B architecture (28 layers, 1024 hidden, 16q/8kv, "
+                       "head_dim 128, vocab 151936, tied head)", "requests_total": wl["batch"],
+                       "prompts": f"uniform {wl['prompt_lo']}..{wl['prompt_hi']}", "new_tokens": n_new,
+                       "parallelism": f"dp{world} by request", "kv_bytes_per_decode_step_mid_run_gpu0": kv_mid},
+            "prefill_tok_s": round(prompt_tokens / (prefill_ms / 1e3), 1),
+            "e2e": {"value": round(value, 1), "unit": "tok/s", "h2d_bytes_per_step": 16 * len(prompts),
+                    "d2h_bytes_per_step": 8 * len(prompts),
+                    "path": "barellm_b200.engine.PagedEngine.generate (token ids in, token ids out)"},
+            "gpu_launches": None,
+            "clocks": sampler.summary(),
+            "first_tokens_req0": out[0][:8] if out else [],
+        }
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -884,7 +962,15 @@ def main() -> None:
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    prefill = WORKLOADS[args.workload].get("kind") == "prefill"
+    kind = WORKLOADS[args.workload].get("kind")
+    prefill = kind == "prefill"
+    if kind == "e2e":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the end-to-end model workload has no CPU port "
+                              "(the reference arm covers the decode and prefill kernels)"}))
+            return
+        run_e2e(args, args.workload)
+        return
     if args.impl == "reference":
         (run_reference_prefill if prefill else run_reference)(args, args.workload)
     else:
