@@ -55,10 +55,11 @@ class CudaPagedAttentionBackend:
     def _batched(self, q, new_k, new_v, layer: BatchLayerKV) -> torch.Tensor:
         meta = layer.append_only(new_k, new_v)
         s = layer.storage()
-        idx = layer.layers[0].layer_idx
+        idx = layer.layer_idx
         if q.shape[2] == 1:
             serial = ops.plan_serial(s.device)
             if meta.plan_ws is None or meta.plan_token != serial or meta.plan_heads != q.shape[1]:
+                # once per step: the plan depends only on the lengths, not the layer
                 meta.plan_ws = ops.paged_decode_plan(s.key_cache, s.value_cache, s.arena.table, meta.seq_lens,
                                                      meta.max_seq_len, q.shape[1], row_ids=meta.rows, err=s.err)
                 meta.plan_token = ops.plan_serial(s.device)

@@ -3,12 +3,13 @@
 Interface of the reference's BatchKVCache / BatchLayerKV
 (src/barellm/engine/batched_kv_cache.py:8-145).  The reference loops over rows
 in Python for every layer (one append and one gather per row) and rebuilds
-lengths and block tables on each call.  Here a step's metadata -- arena row of
-each request, pre-append lengths, post-append lengths -- goes to the device in
-one pinned copy the first time any layer needs it and is shared by every
-layer of the step (all layers of a request advance together); the split-K
-decode plan built from it is shared the same way.  Appends and reads are one
-kernel launch for the whole batch.
+lengths and block tables on each call.  Here the batch resolves its requests
+to arena rows once; per layer, lengths and capacity checks are numpy array
+operations on the pool's length table, the step's metadata (arena rows,
+pre-append and post-append lengths) reaches the device in one pinned copy the
+first time any layer needs it and is shared by every layer of the step, and
+the split-K decode plan built from it is shared the same way.  Appends and
+reads are one kernel launch for the whole batch.
 """
 
 from __future__ import annotations
@@ -21,74 +22,148 @@ from .paged_kv_cache import PagedBatchKVMetadata, PagedKVCache, PagedKVCacheView
 
 
 class StepMeta:
-    """Device metadata for one (pre-append lengths, new tokens) combination."""
+    """Device metadata for one (pre-append lengths, new tokens) combination.
 
-    def __init__(self, storage: PagedKVCache, rows: list[int], starts: list[int], new_tokens: int) -> None:
+    With ``static_max_seq_len`` the device buffers are allocated once and
+    ``refresh`` rewrites them in place (one pinned host-to-device copy), so a
+    captured CUDA graph that reads them stays valid from step to step;
+    ``max_seq_len`` is then the fixed bound the graph was captured with."""
+
+    def __init__(self, storage: PagedKVCache, rows: np.ndarray, starts: np.ndarray, new_tokens: int,
+                 static_max_seq_len: int | None = None) -> None:
         b = len(rows)
-        host = torch.empty((3, b), dtype=torch.int32).pin_memory()
+        host = torch.empty((3, b), dtype=torch.int32)
+        if storage.device.type == "cuda":
+            host = host.pin_memory()
+        self._host = host
         h = host.numpy()
         h[0] = rows
         h[1] = starts
-        h[2] = np.asarray(starts, dtype=np.int64) + new_tokens
-        dev = host.to(storage.device, non_blocking=True)
-        self.rows, self.starts, self.seq_lens = dev[0], dev[1], dev[2]
-        self.seq_lens_host = [s + new_tokens for s in starts]
-        self.max_seq_len = max(self.seq_lens_host)
+        h[2] = starts + new_tokens
+        self._dev = host.to(storage.device, non_blocking=True)
+        self.rows, self.starts, self.seq_lens = self._dev[0], self._dev[1], self._dev[2]
+        self.seq_lens_host = h[2].astype(np.int64)
+        self.static = static_max_seq_len is not None
+        self.max_seq_len = int(static_max_seq_len) if self.static else int(self.seq_lens_host.max())
         self.new_tokens = new_tokens
         self.plan_ws: torch.Tensor | None = None
         self.plan_heads = 0
         self.plan_token = -1
 
+    def matches(self, starts: np.ndarray, new_tokens: int) -> bool:
+        h = self._host.numpy()
+        return new_tokens == self.new_tokens and np.array_equal(h[1], starts)
+
+    def stage(self, starts: np.ndarray, new_tokens: int) -> None:
+        """Static mode, for graph replay: write the next step's lengths into the
+        pinned host buffer only; the captured copy moves them to the device."""
+        h = self._host.numpy()
+        h[1] = starts
+        h[2] = starts + new_tokens
+        self.seq_lens_host = h[2].astype(np.int64)
+        check(int(self.seq_lens_host.max()) <= self.max_seq_len, "sequence grew past the captured bound")
+
+    def refresh(self, starts: np.ndarray, new_tokens: int) -> None:
+        """Static mode: new lengths into the same device buffers (one copy)."""
+        h = self._host.numpy()
+        h[1] = starts
+        h[2] = starts + new_tokens
+        self.seq_lens_host = h[2].astype(np.int64)
+        check(int(self.seq_lens_host.max()) <= self.max_seq_len, "sequence grew past the captured bound")
+        self.new_tokens = new_tokens
+        self._dev.copy_(self._host, non_blocking=True)
+        self.plan_ws = None  # the lengths changed: the plan must be rebuilt
+
 
 class BatchKVCache:
-    def __init__(self, caches: list[PagedKVCacheView]) -> None:
+    """``static_max_seq_len``: keep one set of device metadata buffers for the
+    life of this view (refreshed in place each step) so the decode step can be
+    captured in a CUDA graph; lengths may not exceed the bound."""
+
+    def __init__(self, caches: list[PagedKVCacheView], *, static_max_seq_len: int | None = None) -> None:
         check(len(caches) > 0, "batch cache cannot be empty")
         self.caches = caches
-        self._meta: dict[tuple[tuple[int, ...], int], StepMeta] = {}
+        self._meta: dict[tuple[bytes, int], StepMeta] = {}
+        self._static: StepMeta | None = None
+        first = getattr(caches[0], "storage", None)
+        self.storage: PagedKVCache | None = None
+        if isinstance(first, PagedKVCache) and all(
+            isinstance(c, PagedKVCacheView) and c.storage is first for c in caches
+        ):
+            self.storage = first
+            pages = first.request_pages
+            try:
+                self.rows = np.fromiter((pages[c.request_id].row for c in caches), dtype=np.int64, count=len(caches))
+            except KeyError as exc:
+                raise KeyError(f"Unknown request: {exc.args[0]}") from exc
+            if static_max_seq_len is not None:
+                zeros = np.zeros(len(caches), dtype=np.int64)
+                self._static = StepMeta(first, self.rows, zeros, 0, static_max_seq_len=static_max_seq_len)
 
     def layer(self, layer_idx: int) -> "BatchLayerKV":
-        return BatchLayerKV([cache.layer(layer_idx) for cache in self.caches], owner=self)
+        if self.storage is not None and not 0 <= layer_idx < self.storage.num_layers:
+            raise IndexError(f"Invalid layer index: {layer_idx}")
+        return BatchLayerKV(None, owner=self, layer_idx=layer_idx)
 
-    def step_meta(self, storage: PagedKVCache, rows: list[int], starts: list[int], new_tokens: int) -> StepMeta:
-        key = (tuple(starts), new_tokens)
+    def step_meta(self, starts: np.ndarray, new_tokens: int) -> StepMeta:
+        if self._static is not None:
+            if not self._static.matches(starts, new_tokens):
+                self._static.refresh(starts, new_tokens)
+            return self._static
+        key = (starts.tobytes(), new_tokens)
         meta = self._meta.get(key)
         if meta is None:
-            meta = StepMeta(storage, rows, starts, new_tokens)
+            meta = StepMeta(self.storage, self.rows, starts, new_tokens)
             self._meta = {key: meta}  # one live step per batch view
         return meta
 
 
 class BatchLayerKV:
-    def __init__(self, layers: list[PagedLayerKV], owner: BatchKVCache | None = None) -> None:
-        self.layers = layers
-        self.owner = owner if owner is not None else BatchKVCache([PagedKVCacheView(l.storage, l.request_id) for l in layers])
-        self._storage: PagedKVCache | None = None
+    """One layer of a BatchKVCache.  ``BatchLayerKV(layers)`` also accepts a
+    list of PagedLayerKV of one layer, as the reference's constructor does."""
+
+    def __init__(self, layers: list[PagedLayerKV] | None, owner: BatchKVCache | None = None,
+                 layer_idx: int | None = None) -> None:
+        if owner is None:
+            check(layers is not None and len(layers) > 0, "batch cache cannot be empty")
+            if not all(isinstance(l, PagedLayerKV) for l in layers):
+                raise TypeError("paged metadata requires PagedLayerKV members")
+            owner = BatchKVCache([PagedKVCacheView(l.storage, l.request_id) for l in layers])
+            layer_idx = layers[0].layer_idx
+            if any(l.layer_idx != layer_idx for l in layers):
+                raise ValueError("paged batch layers must share storage and layout")
+        self.owner = owner
+        self.layer_idx = int(layer_idx)
+        self._layers = layers
 
     # -- helpers -------------------------------------------------------------
+    @property
+    def layers(self) -> list:
+        if self._layers is None:
+            self._layers = [c.layer(self.layer_idx) for c in self.owner.caches]
+        return self._layers
+
     def storage(self) -> PagedKVCache:
         """The single paged pool every member must share (TypeError otherwise)."""
-        if self._storage is None:
-            if not all(isinstance(l, PagedLayerKV) for l in self.layers):
-                raise TypeError("paged metadata requires PagedLayerKV members")
-            first = self.layers[0]
-            if any(l.storage is not first.storage or l.layer_idx != first.layer_idx for l in self.layers[1:]):
-                raise ValueError("paged batch layers must share storage and layout")
-            self._storage = first.storage
-        return self._storage
+        s = self.owner.storage
+        if s is None:
+            raise TypeError("paged metadata requires PagedLayerKV members sharing one PagedKVCache")
+        return s
+
+    def starts(self) -> np.ndarray:
+        s = self.storage()
+        return s.arena.lens[self.owner.rows, self.layer_idx]
 
     def meta(self, new_tokens: int) -> StepMeta:
-        s = self.storage()
-        rows = [s.request_pages[l.request_id].row for l in self.layers]
-        starts = [l.seq_len for l in self.layers]
-        return self.owner.step_meta(s, rows, starts, new_tokens)
+        return self.owner.step_meta(self.starts(), new_tokens)
 
     @property
     def lengths(self) -> torch.Tensor:
-        return torch.tensor([l.seq_len for l in self.layers], dtype=torch.long)
+        return torch.from_numpy(self.starts().copy())
 
     @property
     def seq_len(self) -> int:
-        return max(l.seq_len for l in self.layers)
+        return int(self.starts().max())
 
     # -- reference interface ---------------------------------------------------
     def append(self, key: torch.Tensor, value: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
@@ -99,39 +174,46 @@ class BatchLayerKV:
         """One scatter kernel for every row (reference: a Python loop of
         per-row appends, batched_kv_cache.py:40-63).  Returns the step metadata
         whose ``seq_lens`` are the post-append lengths."""
-        check(key.shape[0] == len(self.layers), "batch size must match number of caches")
-        check(value.shape[0] == len(self.layers), "batch size must match number of caches")
+        b = len(self.owner.caches)
+        check(key.shape[0] == b, "batch size must match number of caches")
+        check(value.shape[0] == b, "batch size must match number of caches")
         s = self.storage()
-        self.layers[0].check_new_kv(key, value, batch=len(self.layers))
+        s.check_new_kv(key, value, batch=b)
         t = key.shape[2]
-        for l in self.layers:
-            l.check_capacity(t)
-        meta = self.meta(t)
-        ops.paged_append(s.key_cache, s.value_cache, self.layers[0].layer_idx, s.arena.table, meta.starts, key, value,
+        rows = self.owner.rows
+        starts = s.arena.lens[rows, self.layer_idx]
+        ends = starts + t
+        need = (ends + s.block_size - 1) // s.block_size
+        check(bool((need <= s.arena.used[rows]).all()), "request does not have enough allocated KV blocks")
+        meta = self.owner.step_meta(starts, t)
+        ops.paged_append(s.key_cache, s.value_cache, self.layer_idx, s.arena.table, meta.starts, key, value,
                          row_ids=meta.rows, err=s.err)
-        for l in self.layers:
-            l._request.layer_seq_lens[l.layer_idx] += t
+        s.arena.lens[rows, self.layer_idx] = ends
         return meta
 
     def current_meta(self) -> StepMeta:
         """Metadata whose post-append lengths equal the current lengths."""
-        for (starts, t), meta in self.owner._meta.items():
-            if [a + t for a in starts] == [l.seq_len for l in self.layers]:
+        cur = self.starts()
+        st = self.owner._static
+        if st is not None and np.array_equal(st.seq_lens_host, cur):
+            return st
+        for meta in self.owner._meta.values():
+            if np.array_equal(meta.seq_lens_host, cur):
                 return meta
-        return self.meta(0)
+        return self.owner.step_meta(cur, 0)
 
     def read(self) -> tuple[torch.Tensor, torch.Tensor]:
         """Dense zero-padded ``[B, H, Tmax, D]`` K and V (batched_kv_cache.py:65-95)."""
-        check(all(l.seq_len > 0 for l in self.layers), "KV cache is empty")
+        check(bool((self.starts() > 0).all()), "KV cache is empty")
         s = self.storage()
         meta = self.current_meta()
-        return ops.paged_gather(s.key_cache, s.value_cache, self.layers[0].layer_idx, s.arena.table, meta.seq_lens,
+        return ops.paged_gather(s.key_cache, s.value_cache, self.layer_idx, s.arena.table, meta.seq_lens,
                                 meta.max_seq_len, row_ids=meta.rows, err=s.err)
 
     def attention_mask(self, q_len: int) -> torch.Tensor:
         """``[B, 1, q_len, Tmax]`` valid-key mask (batched_kv_cache.py:97-102)."""
         s = self.storage()
-        lens = torch.tensor([l.seq_len for l in self.layers], dtype=torch.long, device=s.device)
+        lens = torch.from_numpy(self.starts().copy()).to(s.device)
         valid = torch.arange(int(lens.max()), device=s.device).unsqueeze(0) < lens.unsqueeze(1)
         return valid[:, None, None, :].expand(-1, 1, q_len, -1)
 
@@ -139,14 +221,13 @@ class BatchLayerKV:
         """Rectangular int32 block tables padded with -1 and int32 post-append
         lengths (batched_kv_cache.py:104-145), gathered from the arena."""
         s = self.storage()
-        for l in self.layers:
-            check(l.seq_len > 0, "KV cache is empty")
+        check(bool((self.starts() > 0).all()), "KV cache is empty")
         meta = self.current_meta()
-        counts = [len(s.request_pages[l.request_id].blocks) for l in self.layers]
-        width = max(counts)
+        counts = s.arena.used[self.owner.rows]
+        width = int(counts.max())
         tables = s.arena.table.index_select(0, meta.rows.long())[:, :width].clone()
         col = torch.arange(width, device=s.device).unsqueeze(0)
-        limit = torch.tensor(counts, device=s.device).unsqueeze(1)
+        limit = torch.from_numpy(counts.copy()).to(s.device).unsqueeze(1)
         tables.masked_fill_(col >= limit, -1)
-        return PagedBatchKVMetadata(s.key_cache, s.value_cache, self.layers[0].layer_idx, tables, meta.seq_lens.clone(),
+        return PagedBatchKVMetadata(s.key_cache, s.value_cache, self.layer_idx, tables, meta.seq_lens.clone(),
                                     s.block_size)

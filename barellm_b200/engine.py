@@ -177,7 +177,12 @@ class PagedEngine:
         return sum(math.ceil((n + max_new) / block_size) for n in prompt_lens)
 
     @torch.inference_mode()
-    def generate(self, prompts: list[list[int]], max_new_tokens: int, timings: dict | None = None) -> list[list[int]]:
+    def generate(self, prompts: list[list[int]], max_new_tokens: int, timings: dict | None = None,
+                 use_graph: bool = True) -> list[list[int]]:
+        """Greedy generation.  ``use_graph``: after one eager decode step, the
+        decode step (all layers, append + attention kernels, argmax) is captured
+        once as a CUDA graph and replayed; each replay only needs the next
+        tokens, positions and lengths copied in."""
         reqs = [_Request(f"req-{i}", p) for i, p in enumerate(prompts)]
         dev = self.device
         t0 = torch.cuda.Event(enable_timing=True)
@@ -192,16 +197,19 @@ class PagedEngine:
             logits = self.model(ids, pos, kv_cache=self.manager.get_cache(r))
             r.tokens.append(int(torch.argmax(logits[0, -1]).item()))
         t1.record()
-        for _ in range(max_new_tokens - 1):
-            for r in reqs:
-                if not self.manager.allocate_request(r):
-                    raise RuntimeError("KV pool exhausted during decode")
-            ids = torch.tensor([[r.tokens[-1]] for r in reqs], dtype=torch.long, device=dev)
-            pos = torch.tensor([[r.seq_len - 1] for r in reqs], dtype=torch.long, device=dev)
-            logits = self.model(ids, pos, kv_cache=BatchKVCache([self.manager.get_cache(r) for r in reqs]))
-            nxt = torch.argmax(logits[:, -1], dim=-1).tolist()
-            for r, tok in zip(reqs, nxt):
-                r.tokens.append(int(tok))
+        if use_graph and max_new_tokens > 2:
+            self._decode_graph(reqs, max_new_tokens - 1)
+        else:
+            for _ in range(max_new_tokens - 1):
+                for r in reqs:
+                    if not self.manager.allocate_request(r):
+                        raise RuntimeError("KV pool exhausted during decode")
+                ids = torch.tensor([[r.tokens[-1]] for r in reqs], dtype=torch.long, device=dev)
+                pos = torch.tensor([[r.seq_len - 1] for r in reqs], dtype=torch.long, device=dev)
+                logits = self.model(ids, pos, kv_cache=BatchKVCache([self.manager.get_cache(r) for r in reqs]))
+                nxt = torch.argmax(logits[:, -1], dim=-1).tolist()
+                for r, tok in zip(reqs, nxt):
+                    r.tokens.append(int(tok))
         t2.record()
         torch.cuda.synchronize(dev)
         self.cache.check_device_errors()
@@ -213,3 +221,62 @@ class PagedEngine:
         for r in reqs:
             self.manager.free_request(r.id)
         return out
+
+    def _decode_graph(self, reqs: list[_Request], steps: int) -> None:
+        dev = self.device
+        b = len(reqs)
+        # every block the decode will need, up front: the captured kernels hold
+        # the block-table pointer, so the arena must not grow afterwards
+        final = [_Request(r.id, r.tokens + [0] * (steps - 1)) for r in reqs]
+        for r in final:
+            if not self.manager.allocate_request(r):
+                raise RuntimeError("KV pool exhausted during decode")
+        bound = max(len(r.tokens) for r in final)
+        batch = BatchKVCache([self.manager.get_cache(r) for r in reqs], static_max_seq_len=bound)
+        rows = batch.rows
+        lens = self.cache.arena.lens
+        ids_h = torch.empty((b, 1), dtype=torch.long).pin_memory()
+        pos_h = torch.empty((b, 1), dtype=torch.long).pin_memory()
+        ids_d = torch.empty((b, 1), dtype=torch.long, device=dev)
+        pos_d = torch.empty((b, 1), dtype=torch.long, device=dev)
+        nxt_d = torch.empty((b,), dtype=torch.long, device=dev)
+
+        def stage_inputs():
+            ids_h[:, 0] = torch.tensor([r.tokens[-1] for r in reqs])
+            pos_h[:, 0] = torch.from_numpy(lens[rows, 0].copy())
+            ids_d.copy_(ids_h, non_blocking=True)
+            pos_d.copy_(pos_h, non_blocking=True)
+
+        def body():
+            logits = self.model(ids_d, pos_d, kv_cache=batch)
+            nxt_d.copy_(torch.argmax(logits[:, -1], dim=-1))
+
+        def take():
+            for r, tok in zip(reqs, nxt_d.tolist()):
+                r.tokens.append(int(tok))
+
+        # step 1 eager: sizes the workspace, warms cuBLAS and the allocator
+        stage_inputs()
+        body()
+        take()
+        if steps == 1:
+            return
+        # step 2 captured (capturing runs the host side, advancing lengths),
+        # then replayed to execute it
+        stage_inputs()
+        graph = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side), torch.cuda.graph(graph, stream=side):
+            body()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        graph.replay()
+        take()
+        meta = batch._static
+        for _ in range(steps - 2):
+            meta.stage(lens[rows, 0].copy(), 1)
+            stage_inputs()
+            graph.replay()
+            lens[rows, :] += 1
+            take()
+        del graph

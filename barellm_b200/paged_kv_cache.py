@@ -40,10 +40,12 @@ class BlockTableArena:
     table so a growth uploads only the entries that changed, asynchronously
     from pinned memory on the current stream."""
 
-    def __init__(self, device: torch.device, rows: int = 64, width: int = 64) -> None:
+    def __init__(self, device: torch.device, rows: int = 64, width: int = 64, num_layers: int = 1) -> None:
         self.device = device
         self.host = np.full((rows, width), -1, dtype=np.int32)
         self.used = np.zeros(rows, dtype=np.int64)  # valid entries per row
+        # per-row, per-layer cached lengths (host side); rows index the table
+        self.lens = np.zeros((rows, num_layers), dtype=np.int64)
         self.table = torch.full((rows, width), -1, dtype=torch.int32, device=device)
         self._free_rows = list(range(rows - 1, -1, -1))
 
@@ -60,15 +62,19 @@ class BlockTableArena:
         table[:r0, :w0].copy_(self.table)
         self.host, self.table = host, table
         self.used = np.concatenate([self.used, np.zeros(r1 - r0, dtype=np.int64)])
+        self.lens = np.concatenate([self.lens, np.zeros((r1 - r0, self.lens.shape[1]), dtype=np.int64)])
         self._free_rows = list(range(r1 - 1, r0 - 1, -1)) + self._free_rows
 
     def alloc_row(self) -> int:
         if not self._free_rows:
             self._grow(rows=2 * self.host.shape[0])
-        return self._free_rows.pop()
+        row = self._free_rows.pop()
+        self.lens[row] = 0
+        return row
 
     def free_row(self, row: int) -> None:
         self.used[row] = 0
+        self.lens[row] = 0
         self._free_rows.append(row)
 
     def set_row(self, row: int, block_ids: list[int]) -> None:
@@ -99,8 +105,12 @@ class BlockTableArena:
 class _RequestPages:
     blocks: list[KVCacheBlock]
     row: int
-    layer_seq_lens: list[int]
     arena: BlockTableArena = field(repr=False)
+
+    @property
+    def layer_seq_lens(self) -> np.ndarray:
+        """Cached length per layer (a writable view into the arena's table)."""
+        return self.arena.lens[self.row]
 
     @property
     def block_table(self) -> torch.Tensor:
@@ -164,7 +174,7 @@ class PagedKVCache:
         self.value_cache = torch.empty_like(self.key_cache)
         self.device = self.key_cache.device
         self.request_pages: dict[str, _RequestPages] = {}
-        self.arena = BlockTableArena(self.device, rows=max_requests, width=64)
+        self.arena = BlockTableArena(self.device, rows=max_requests, width=64, num_layers=num_layers)
         self._err = None
 
     # -- error word shared by this pool's kernels -------------------------
@@ -188,11 +198,24 @@ class PagedKVCache:
     def register_request(self, request_id: str, blocks: list[KVCacheBlock]) -> None:
         pages = self.request_pages.get(request_id)
         if pages is None:
-            pages = _RequestPages(list(blocks), self.arena.alloc_row(), [0] * self.num_layers, self.arena)
+            pages = _RequestPages(list(blocks), self.arena.alloc_row(), self.arena)
             self.request_pages[request_id] = pages
         else:
             pages.blocks = list(blocks)
         self.arena.set_row(pages.row, [b.block_id for b in blocks])
+
+    def check_new_kv(self, key: torch.Tensor, value: torch.Tensor, batch: int = 1) -> None:
+        """The reference's append checks (paged_kv_cache.py:156-174)."""
+        check(key.ndim == 4 and value.ndim == 4, "K/V must have shape [B, H, T, D]")
+        check(key.shape == value.shape, "K/V must have identical shape")
+        check(key.shape[0] == batch, "PagedKVCache currently supports batch size 1")
+        check(key.shape[1] == self.num_kv_heads, "KV-head count cannot change")
+        check(key.shape[2] > 0, "K/V sequence length must be greater than zero")
+        check(key.shape[3] == self.head_dim, "Head dimension cannot change")
+        check(key.dtype == self.dtype, "K/V dtype cannot change")
+        check(key.device == self.device, "K/V device cannot change")
+        check(key.dtype == value.dtype, "K/V dtype must match")
+        check(key.device == value.device, "K/V device must match")
 
     def unregister_request(self, request_id: str) -> None:
         pages = self.request_pages.pop(request_id, None)
@@ -236,25 +259,14 @@ class PagedLayerKV:
 
     @property
     def seq_len(self) -> int:
-        return self._request.layer_seq_lens[self.layer_idx]
+        return int(self._request.layer_seq_lens[self.layer_idx])
 
     def append(self, key: torch.Tensor, value: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         self.append_only(key, value)
         return self.read()
 
     def check_new_kv(self, key: torch.Tensor, value: torch.Tensor, batch: int = 1) -> None:
-        """The reference's append checks (paged_kv_cache.py:156-174)."""
-        s = self.storage
-        check(key.ndim == 4 and value.ndim == 4, "K/V must have shape [B, H, T, D]")
-        check(key.shape == value.shape, "K/V must have identical shape")
-        check(key.shape[0] == batch, "PagedKVCache currently supports batch size 1")
-        check(key.shape[1] == s.num_kv_heads, "KV-head count cannot change")
-        check(key.shape[2] > 0, "K/V sequence length must be greater than zero")
-        check(key.shape[3] == s.head_dim, "Head dimension cannot change")
-        check(key.dtype == s.dtype, "K/V dtype cannot change")
-        check(key.device == s.device, "K/V device cannot change")
-        check(key.dtype == value.dtype, "K/V dtype must match")
-        check(key.device == value.device, "K/V device must match")
+        self.storage.check_new_kv(key, value, batch)
 
     def check_capacity(self, new_tokens: int) -> None:
         end = self.seq_len + new_tokens
@@ -266,7 +278,7 @@ class PagedLayerKV:
         self.check_capacity(key.shape[2])
         s = self.storage
         req = self._request
-        start = req.layer_seq_lens[self.layer_idx]
+        start = int(req.layer_seq_lens[self.layer_idx])
         ops.paged_append(s.key_cache, s.value_cache, self.layer_idx, s.arena.table,
                          _i32([start], s.device), key, value, row_ids=_i32([req.row], s.device), err=s.err)
         req.layer_seq_lens[self.layer_idx] = start + key.shape[2]

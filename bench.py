@@ -350,7 +350,7 @@ def e2e_measure(wl: dict, work: DecodeWorkload, steps: int, warmup: int, device)
         v_d.copy_(v_h, non_blocking=True)
         layer = BatchKVCache(views).layer(0)
         out = backend.attend(q_d, k_d, v_d, layer, hq // hkv)
-        seq_hist.append([l.seq_len for l in layer.layers])
+        seq_hist.append(layer.starts().tolist())
         out_h.copy_(out, non_blocking=True)
 
     for _ in range(warmup):

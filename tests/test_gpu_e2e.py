@@ -36,6 +36,17 @@ def test_fp32_paged_engine_matches_contiguous_oracle_exactly(cuda, native_lib):
     assert got == want
 
 
+def test_graph_decode_matches_eager_decode(cuda, native_lib):
+    """The CUDA-graph decode loop replays exactly what the eager loop runs."""
+    shape = Qwen3Shape(vocab_size=1024, num_layers=3)
+    model = random_qwen3(shape, dtype=torch.bfloat16, device=cuda, seed=11)
+    prompts = prompts_for(5, 10, 200, shape.vocab_size, seed=12)
+    blocks = PagedEngine.blocks_needed([len(p) for p in prompts], 20, 16) + 4
+    eager = PagedEngine(model, num_blocks=blocks).generate(prompts, 20, use_graph=False)
+    graph = PagedEngine(model, num_blocks=blocks).generate(prompts, 20, use_graph=True)
+    assert eager == graph
+
+
 def test_fp32_uncached_recompute_matches_cached_decode(cuda, native_lib):
     """The reference's cached-vs-uncached greedy identity, with every forward
     (uncached: the full sequence each step) through the CUDA backend."""
