@@ -2,28 +2,29 @@
 // tensor memory), bf16 / fp16, head_dim 128, block_size 16, GQA group G in
 // {1, 2, 4, 8}.
 //
-// A CTA owns 128 score rows = (128 / G) query tokens x the G query heads that
-// share one KV head (head-major: row r = head (r / bq), token (r % bq)), so
-// every K/V page is fetched once for the whole GQA group.  Keys are consumed
-// in tiles of 128 (8 pages).  Warp roles:
-//   warp 0      TMA producer: K and V pages of a tile, each page two 64 x 16
-//               boxes with the 128-byte swizzle, into a 2-stage ring with
-//               separate K and V slots.  K runs a tile ahead of V: a K slot is
-//               recycled as soon as its S = Q K^T MMAs finish, a V slot only
-//               after its P V MMAs.  Pages past the row's last page are fetched
+// A CTA owns 256 score rows = (256 / G) query tokens x the G query heads that
+// share one KV head, as two 128-row tiles A and B (head-major rows, so for
+// G >= 2 both tiles cover the same tokens and need the same keys).  Every K/V
+// page is fetched once for 256 rows, which halves the K/V bytes per flop of a
+// 128-row tile; keys are consumed in tiles of 128 (8 pages).  Warp roles:
+//   warp 0      TMA producer: K and V pages of a key tile, each page two 64 x 16
+//               boxes with the 128-byte swizzle, into 2-stage K and V rings.  K
+//               runs a tile ahead of V (K slots free up after Q K^T, V slots
+//               only after P V).  Pages past the row's last page are fetched
 //               from out-of-range coordinates, which TMA fills with zeros.
-//   warp 1      TMEM owner (512 columns: S double buffer at 0 / 128, O at 256)
-//               and, on one lane, the MMA issuer: S_t = Q K_t^T (M 128, N 128,
-//               8 x K16, both operands K-major) into S[t % 2], then
-//               O += P_{t-1} V_{t-1} (P K-major from shared memory, V MN-major).
-//   warps 2..9  softmax + epilogue, two threads per score row (= TMEM lane),
-//               each owning 64 of its columns; per tile they exchange only the
-//               row max.  tcgen05.ld the S half-row, scale to log2 units,
-//               bottom-right causal mask, online softmax with a lazy rescale (O
-//               in TMEM is rescaled only when the running max grows by more
-//               than 2^8), exponentials computed while the previous P V still
-//               runs, P as bf16/fp16 into the swizzled shared P tile; finally
-//               O / l from TMEM to global memory.
+//   warp 1      TMEM owner (512 columns: S_A 0..127, S_B 128..255, O_A 256..383,
+//               O_B 384..511) and, on one lane, the MMA issuer.  Per key tile t:
+//               O_A += P_A V_{t-1}, O_B += P_B V_{t-1}, then S_A = Q_A K_t^T,
+//               S_B = Q_B K_t^T; S_X is rewritten only after the P V that read
+//               P_X (stored in S_X's columns) has completed, and the two tiles
+//               interleave so one tile's softmax overlaps the other's MMAs.
+//   warps 2..5  softmax of tile A, warps 6..9 of tile B: one thread per score
+//               row (= TMEM lane).  Pass 1 reads the S row from TMEM for the
+//               row max (scale to log2 units, bottom-right causal mask); a lazy
+//               rescale touches O only when the max grows by more than 2^8;
+//               pass 2 re-reads S, exponentiates and writes P as packed
+//               bf16/fp16 back into the S columns, where the P V MMA reads it
+//               as its A operand.  Epilogue: O / l from TMEM to global memory.
 // Every mbarrier wait is bounded; on a time-out the CTA records
 // BL_DEVERR_TIMEOUT, drains what it issued and frees its TMEM.
 // Roofline: tensor.  Algorithmic flops per request: 4 * Hq * D * (C*P + C(C+1)/2).
@@ -38,21 +39,20 @@ constexpr int kD = 128;
 constexpr int kBS = 16;
 constexpr int kKT = 128;                 // keys per tile
 constexpr int kPPT = kKT / kBS;          // 8 pages per tile
-constexpr int kRows = 128;               // score rows per CTA (MMA M)
+constexpr int kTileRows = 128;           // rows per MMA tile (M)
+constexpr int kRows = 2 * kTileRows;     // score rows per CTA
 constexpr int kStages = 2;
-constexpr int kThreads = 320;            // producer, MMA, 8 softmax warps
-constexpr int kSoftmaxThreads = 256;
+constexpr int kThreads = 320;            // producer, MMA, 2 x 4 softmax warps
 constexpr int kHalf = 128 * 128;         // 16 KB: 128 rows x 128 B (64 elements of D or K)
 constexpr int kTile = 2 * kHalf;         // 32 KB
 constexpr int kPageHalf = kBS * 128;     // 2 KB: 16 rows x 128 B
-constexpr int kOffQ = 0;
-constexpr int kOffK = kTile;                    // + s * kTile
+constexpr int kOffQ = 0;                        // + X * kTile
+constexpr int kOffK = 2 * kTile;                // + s * kTile
 constexpr int kOffV = kOffK + kStages * kTile;  // + s * kTile
-constexpr int kOffP = kOffV + kStages * kTile;
-constexpr int kSmemData = kOffP + kTile;        // 192 KB
+constexpr int kSmemData = kOffV + kStages * kTile;  // 192 KB
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS = 0;                   // + buffer * 128
-constexpr uint32_t kColO = 256;
+constexpr uint32_t kColS = 0;                   // + X * 128 (P_X aliases the first 64 columns)
+constexpr uint32_t kColO = 256;                 // + X * 128
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;       // log2 units
 
@@ -67,7 +67,7 @@ struct Args {
   int64_t bt_stride;
   int32_t bt_width;
   const int32_t* row_ids;
-  int32_t hkv, g, bq;
+  int32_t hkv, g, bq;  // bq = query tokens per CTA = kRows / g
   int64_t num_blocks, layer_row0, max_q;
   int32_t rows_total;  // rows of the pool tensor map: an out-of-range coordinate
   float scale_log2;
@@ -76,7 +76,7 @@ struct Args {
 
 struct Shared {
   uint64_t full_k[kStages], full_v[kStages], empty_k[kStages], empty_v[kStages];
-  uint64_t s_full[2], s_free[2], p_full, pv_done, q_full, mma_done;
+  uint64_t s_full[2], p_full[2], pv_done[2], q_full, mma_done;
   uint32_t tmem_base;
   int abort;
 };
@@ -98,7 +98,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Shared* sh = reinterpret_cast<Shared*>(smem + kSmemData);
 
-  // ---- which 128 rows: heaviest q tiles first ----
+  // ---- which rows: heaviest query tiles first ----
   const int64_t qtile = (int64_t)gridDim.x - 1 - blockIdx.x;
   const int h = blockIdx.y;
   const int64_t b = blockIdx.z;
@@ -126,13 +126,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&sh->empty_k[s], 1);
       mbar_init(&sh->empty_v[s], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&sh->s_full[i], 1);
-      mbar_init(&sh->s_free[i], kSoftmaxThreads);
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(&sh->s_full[x], 1);
+      mbar_init(&sh->p_full[x], kTileRows);
+      mbar_init(&sh->pv_done[x], 1);
     }
-    mbar_init(&sh->p_full, kSoftmaxThreads);
-    mbar_init(&sh->pv_done, 1);
-    mbar_init(&sh->q_full, kSoftmaxThreads);
+    mbar_init(&sh->q_full, kRows);
     mbar_init(&sh->mma_done, 1);
     sh->abort = 0;
     fence_mbar_init();
@@ -152,7 +151,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t row = a.row_ids ? (int64_t)a.row_ids[b] : b;
       const int32_t* bt = a.block_tables + row * a.bt_stride;
       int issued_k = 0, issued_v = 0;
-      auto page_rows = [&](int t, int32_t(&ys)[kPPT]) {
+      auto load = [&](const CUtensorMap* map, uint64_t* full, unsigned char* dst, int t) {
+        int32_t ys[kPPT];
+#pragma unroll
         for (int p = 0; p < kPPT; ++p) {
           const int lb = t * kPPT + p;
           if (lb < npages) {
@@ -166,18 +167,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             ys[p] = a.rows_total;  // fully out of range: TMA writes zeros
           }
         }
-      };
-      auto load = [&](const CUtensorMap* map, uint64_t* full, unsigned char* dst, int t) {
-        int32_t ys[kPPT];
-        page_rows(t, ys);
         mbar_arrive_expect_tx(full, kTile);
+#pragma unroll
         for (int p = 0; p < kPPT; ++p) {
           tma_load_2d(dst + p * kPageHalf, map, full, 0, ys[p]);
           tma_load_2d(dst + kHalf + p * kPageHalf, map, full, 64, ys[p]);
         }
       };
-      // K runs one tile ahead of V: K slots free up right after S = Q K^T,
-      // V slots only after P V, so waiting on a V slot must not hold back K.
       for (int t = 0; t <= ntiles; ++t) {
         if (t < ntiles) {
           const int s = t & 1;
@@ -207,44 +203,48 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------ MMA issuer ------------------------------
     if (lane == 0) {
-      const uint32_t idesc_s = umma_idesc_f16(kRows, kKT, BF16, false);
-      const uint32_t idesc_o = umma_idesc_f16(kRows, kD, BF16, true);
-      const uint32_t sq = smem_u32(smem + kOffQ);
-      const uint32_t sp = smem_u32(smem + kOffP);
+      const uint32_t idesc_s = umma_idesc_f16(kTileRows, kKT, BF16, false);
+      const uint32_t idesc_o = umma_idesc_f16(kTileRows, kD, BF16, true);
       bool ok = wait_or_abort(&sh->q_full, 0, sh, a.err);
-      auto issue_pv = [&](int j) -> bool {
+      if (ok) tc_fence_after();
+      auto issue_pv = [&](int j) -> bool {  // O_X += P_X V_j for both tiles
         const int s = j & 1;
         if (!wait_or_abort(&sh->full_v[s], (j >> 1) & 1, sh, a.err)) return false;
-        if (!wait_or_abort(&sh->p_full, j & 1, sh, a.err)) return false;
-        tc_fence_after();
         const uint32_t sv = smem_u32(smem + kOffV + s * kTile);
+        for (int x = 0; x < 2; ++x) {
+          if (!wait_or_abort(&sh->p_full[x], j & 1, sh, a.err)) return false;
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < kKT / 16; ++kk) {
-          const uint64_t da = umma_desc_sw128(sp + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
-          const uint64_t db = umma_desc_sw128(sv + kk * 2048, kHalf, 1024);
-          tc_mma_ss(tmem + kColO, da, db, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < kKT / 16; ++kk) {
+            const uint64_t db = umma_desc_sw128(sv + kk * 2048, kHalf, 1024);
+            tc_mma_ts(tmem + kColO + x * 128, tmem + kColS + x * 128 + kk * 8, db, idesc_o,
+                      (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(&sh->pv_done[x]);
         }
-        tc_commit(&sh->pv_done);
         tc_commit(&sh->empty_v[s]);
         return true;
       };
-      if (ok) tc_fence_after();
       for (int t = 0; t < ntiles && ok; ++t) {
+        if (t >= 1 && !(ok = issue_pv(t - 1))) break;
         const int s = t & 1;
-        ok = wait_or_abort(&sh->full_k[s], (t >> 1) & 1, sh, a.err) &&
-             wait_or_abort(&sh->s_free[s], ((t >> 1) & 1) ^ 1, sh, a.err);
-        if (!ok) break;
-        tc_fence_after();
+        if (!(ok = wait_or_abort(&sh->full_k[s], (t >> 1) & 1, sh, a.err))) break;
         const uint32_t sk = smem_u32(smem + kOffK + s * kTile);
+        for (int x = 0; x < 2; ++x) {
+          // S_X is rewritten only after the P V that read P_X from it is done
+          if (t >= 1 && !(ok = wait_or_abort(&sh->pv_done[x], (t - 1) & 1, sh, a.err))) break;
+          tc_fence_after();
+          const uint32_t sq = smem_u32(smem + kOffQ + x * kTile);
 #pragma unroll
-        for (int ks = 0; ks < kD / 16; ++ks) {
-          const uint32_t off = (ks >> 2) * kHalf + (ks & 3) * 32;
-          tc_mma_ss(tmem + kColS + s * kKT, umma_desc_sw128(sq + off, 16, 1024), umma_desc_sw128(sk + off, 16, 1024),
-                    idesc_s, ks > 0 ? 1u : 0u);
+          for (int ks = 0; ks < kD / 16; ++ks) {
+            const uint32_t off = (ks >> 2) * kHalf + (ks & 3) * 32;
+            tc_mma_ss(tmem + kColS + x * 128, umma_desc_sw128(sq + off, 16, 1024),
+                      umma_desc_sw128(sk + off, 16, 1024), idesc_s, ks > 0 ? 1u : 0u);
+          }
+          tc_commit(&sh->s_full[x]);
         }
-        tc_commit(&sh->s_full[s]);
+        if (!ok) break;
         tc_commit(&sh->empty_k[s]);
-        if (t >= 1) ok = issue_pv(t - 1);
       }
       if (ok && ntiles > 0) ok = issue_pv(ntiles - 1);
       // every MMA issued here has finished before the CTA tears down
@@ -253,160 +253,130 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------ softmax ------------------------------
-    // Two threads per score row: warps w and w+4 share the TMEM lane group
-    // (w % 4) and split the row's 128 columns (keys of S / dims of O) in two
-    // halves; only the row max is exchanged per tile.
-    const int sw = warp - 2;                // 0..7
-    const int half = sw >> 2;               // 0: columns 0-63, 1: columns 64-127
-    const int grp = warp & 3;               // TMEM lane group
-    const int r = 32 * grp + lane;          // score row == TMEM lane
-    const uint32_t tl = tmem + ((uint32_t)(32 * grp) << 16) + half * 64;
-    float* red = reinterpret_cast<float*>(sh + 1);          // [2][kRows] partial maxima / sums
-    int* red_ok = reinterpret_cast<int*>(red + 2 * kRows);  // [2][kRows]
-    const int pair_bar = 2 + grp;           // named barrier shared by the two warps of a row group
+    const int x = (warp - 2) >> 2;        // tile: 0 = A, 1 = B
+    const int grp = warp & 3;             // TMEM lane group
+    const int tr = 32 * grp + lane;       // row within the tile == TMEM lane
+    const int r = x * kTileRows + tr;     // row within the CTA
+    const uint32_t tl = tmem + ((uint32_t)(32 * grp) << 16);
+    const uint32_t sc = kColS + x * 128, oc = kColO + x * 128;
     const int hd = r / a.bq;
     const int tok = r - hd * a.bq;
     const int64_t qi = q0 + tok;
     const bool valid = qi < nq;
     const int hq = h * a.g + hd;
     const int64_t lim = prefix + qi;  // inclusive key limit
-    // this thread's half of the Q row -> shared memory (K-major, 128-byte swizzle)
+    // Q row -> shared memory (K-major, 128-byte swizzle)
     {
       const T* qrow = reinterpret_cast<const T*>(a.q) + b * a.q_sb + (qo + (valid ? qi : 0)) * a.q_st +
-                      (int64_t)hq * a.q_sh + half * 64;
+                      (int64_t)hq * a.q_sh;
+      unsigned char* qs = smem + kOffQ + x * kTile + tr * 128;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
+      for (int c = 0; c < 16; ++c) {
         uint4 v = make_uint4(0, 0, 0, 0);
         if (valid) {
           const uint32_t* src = reinterpret_cast<const uint32_t*>(qrow + c * 8);
           v = make_uint4(src[0], src[1], src[2], src[3]);
         }
-        *reinterpret_cast<uint4*>(smem + kOffQ + half * kHalf + r * 128 + ((c ^ (r & 7)) << 4)) = v;
+        *reinterpret_cast<uint4*>(qs + (c >> 3) * kHalf + (((c & 7) ^ (tr & 7)) << 4)) = v;
       }
     }
     fence_proxy_async_smem();
     mbar_arrive(&sh->q_full);
 
-    // A failed (timed-out) wait never makes one warp of a pair leave the loop
-    // early: both always reach the pair barriers, agree on the failure there,
-    // and skip the remaining work together.
     float m_used = -INFINITY, l = 0.f;
-    bool failed = false;
+    bool ok = true;
     for (int t = 0; t < ntiles; ++t) {
-      const int s = t & 1;
-      bool ok = !failed && __all_sync(0xffffffffu, wait_or_abort(&sh->s_full[s], (t >> 1) & 1, sh, a.err));
-      float x[64];
+      ok = __all_sync(0xffffffffu, wait_or_abort(&sh->s_full[x], t & 1, sh, a.err));
+      if (!ok) break;
+      tc_fence_after();
+      const int64_t k0 = (int64_t)t * kKT;
+      const bool masked = k0 + kKT - 1 > lim;
+      // pass 1: row max (S_X is complete, and so is the P V that last read it)
       float mt = -INFINITY;
-      const int64_t k0 = (int64_t)t * kKT + half * 64;
-      if (ok) {
-        tc_fence_after();
-        tc_ld32f(tl + kColS + s * kKT, x);
-        tc_ld32f(tl + kColS + s * kKT + 32, x + 32);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tc_ld32f(tl + sc + c * 32, v);
         tc_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 64; ++j) x[j] *= a.scale_log2;
-        tc_fence_before();
-        mbar_arrive(&sh->s_free[s]);
-        if (k0 + 63 > lim) {
-#pragma unroll
-          for (int j = 0; j < 64; ++j)
-            if (k0 + j > lim) x[j] = -INFINITY;
+        for (int j = 0; j < 32; ++j) {
+          const float y = (masked && k0 + c * 32 + j > lim) ? -INFINITY : v[j] * a.scale_log2;
+          mt = fmaxf(mt, y);
         }
-#pragma unroll
-        for (int j = 0; j < 64; ++j) mt = fmaxf(mt, x[j]);
-      }
-      red[half * kRows + r] = mt;
-      red_ok[half * kRows + r] = ok ? 1 : 0;
-      named_barrier_sync(pair_bar, 64);
-      mt = fmaxf(mt, red[(half ^ 1) * kRows + r]);
-      ok = ok && red_ok[(half ^ 1) * kRows + r] != 0;
-      named_barrier_sync(pair_bar, 64);  // the slots are rewritten next tile
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) {
-        failed = true;
-        continue;
       }
       const float m_new = fmaxf(m_used, mt);
       const bool need = (t > 0) && (m_new > m_used + kRescaleThreshold);
-      // the exponentials need only the new max, so they overlap the previous
-      // tile's P V; O and the P buffer are touched only after it completes
       const float alpha = need ? fast_exp2(m_used - m_new) : 1.f;
       if (need || t == 0) m_used = m_new;
       const float ms = (m_used == -INFINITY) ? 0.f : m_used;
-      float rs = 0.f;
-#pragma unroll
-      for (int j = 0; j < 64; ++j) {
-        x[j] = fast_exp2(x[j] - ms);
-        rs += x[j];
-      }
-      l = l * alpha + rs;
-      if (t >= 1) {
-        if (!__all_sync(0xffffffffu, wait_or_abort(&sh->pv_done, (t - 1) & 1, sh, a.err))) {
-          failed = true;
-          continue;
-        }
-        tc_fence_after();
-      }
-      // P (keys of this half) into the half of the swizzled P tile it owns;
-      // packing first frees the fp32 row before O is rescaled
-      unsigned char* prow = smem + kOffP + half * kHalf + r * 128;
-      uint32_t pk[32];
-#pragma unroll
-      for (int e = 0; e < 32; ++e) pk[e] = pack2<T>(x[2 * e], x[2 * e + 1]);
-#pragma unroll
-      for (int c = 0; c < 8; ++c)
-        *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) =
-            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
       if (__any_sync(0xffffffffu, need)) {
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          tc_ld32f(tl + kColO + c * 32, x);
+        for (int c = 0; c < 4; ++c) {
+          float v[32];
+          tc_ld32f(tl + oc + c * 32, v);
           tc_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 32; ++j) x[j] *= alpha;
-          tc_st32f(tl + kColO + c * 32, x);
+          for (int j = 0; j < 32; ++j) v[j] *= alpha;
+          tc_st32f(tl + oc + c * 32, v);
         }
-        tc_wait_st();
       }
+      // pass 2: P = exp2(s - m) packed back over S (chunk c of P lands in
+      // columns already read: 16c .. 16c+15 <= 32c + 31)
+      float rs = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tc_ld32f(tl + sc + c * 32, v);
+        tc_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int k = c * 32 + 2 * j;
+          const float y0 = (masked && k0 + k > lim) ? -INFINITY : v[2 * j] * a.scale_log2;
+          const float y1 = (masked && k0 + k + 1 > lim) ? -INFINITY : v[2 * j + 1] * a.scale_log2;
+          const float p0 = fast_exp2(y0 - ms), p1 = fast_exp2(y1 - ms);
+          rs += p0 + p1;
+          pk[j] = pack2<T>(p0, p1);
+        }
+        tc_st16(tl + sc + c * 16, pk);
+      }
+      tc_wait_st();
+      l = l * alpha + rs;
       // Pool slots past the row length hold stale bytes (possibly NaN): P is 0
-      // there but 0 * NaN is NaN, so zero those V rows of the last tile.
-      if (t == ntiles - 1) {
-        const int first_bad = (int)(len - (int64_t)t * kKT);
+      // there but 0 * NaN is NaN, so tile A's threads zero those V rows of the
+      // last key tile before P_A is published (P V of tile B is issued after A's).
+      if (x == 0 && t == ntiles - 1) {
+        const int first_bad = (int)(len - k0);
         const int last_real = min(npages * kBS - t * kKT, kKT);
         if (first_bad < last_real) {
-          if (!__all_sync(0xffffffffu, wait_or_abort(&sh->full_v[s], (t >> 1) & 1, sh, a.err))) {
-            failed = true;
-            continue;
-          }
+          const int s = t & 1;
+          ok = __all_sync(0xffffffffu, wait_or_abort(&sh->full_v[s], (t >> 1) & 1, sh, a.err));
+          if (!ok) break;
           unsigned char* vs = smem + kOffV + s * kTile;
           const int nchunks = (last_real - first_bad) * 16;  // rows x (2 halves x 8 chunks)
-          for (int e = sw * 32 + lane; e < nchunks; e += kSoftmaxThreads) {
+          for (int e = tr; e < nchunks; e += kTileRows) {
             const int row_k = first_bad + e / 16;
             const int rem = e % 16;
             *reinterpret_cast<uint4*>(vs + (rem >> 3) * kHalf + row_k * 128 + ((rem & 7) << 4)) =
                 make_uint4(0, 0, 0, 0);
           }
+          fence_proxy_async_smem();
         }
       }
-      fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(&sh->p_full);
+      mbar_arrive(&sh->p_full[x]);
     }
-    // ---- epilogue: this thread's 64 output dims ----
-    red[kRows * half + r] = l;
-    named_barrier_sync(pair_bar, 64);
-    const float lt = l + red[kRows * (half ^ 1) + r];
-    if (!failed && ntiles > 0) {
-      const bool ok = __all_sync(0xffffffffu, wait_or_abort(&sh->pv_done, (ntiles - 1) & 1, sh, a.err));
+    // ---- epilogue ----
+    if (ok && ntiles > 0) {
+      ok = __all_sync(0xffffffffu, wait_or_abort(&sh->pv_done[x], (ntiles - 1) & 1, sh, a.err));
       if (ok) {
         tc_fence_after();
-        const float inv = lt > 0.f ? 1.f / lt : 0.f;
-        T* orow = reinterpret_cast<T*>(a.out) + b * a.o_sb + (qo + (valid ? qi : 0)) * a.o_st + (int64_t)hq * a.o_sh +
-                  half * 64;
-        float o[32];
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        T* orow = reinterpret_cast<T*>(a.out) + b * a.o_sb + (qo + (valid ? qi : 0)) * a.o_st + (int64_t)hq * a.o_sh;
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          tc_ld32f(tl + kColO + c * 32, o);
+        for (int c = 0; c < 4; ++c) {
+          float o[32];
+          tc_ld32f(tl + oc + c * 32, o);
           tc_wait_ld();
           if (valid) {
 #pragma unroll
@@ -426,7 +396,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-size_t smem_bytes() { return 1024 + kSmemData + sizeof(Shared) + 4 * kRows * sizeof(float); }
+size_t smem_bytes() { return 1024 + kSmemData + sizeof(Shared); }
 
 template <bool BF16>
 int launch(const bl_prefill_args& a, cudaStream_t s) {
