@@ -352,6 +352,15 @@ __device__ __forceinline__ void tc_st16(uint32_t taddr, const uint32_t* r) {
 }
 
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// tcgen05.ld writes its registers asynchronously; the compiler sees them as
+// written at the load.  Passing them through an empty volatile asm placed after
+// tcgen05.wait::ld makes every later use depend on a value defined after the wait.
+template <int N>
+__device__ __forceinline__ void reg_fence(float* r) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+f"(r[i]));
+}
 __device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // ----------------------------------------------------------------------------

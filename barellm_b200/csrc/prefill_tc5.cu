@@ -13,18 +13,18 @@
 //               only after P V).  Pages past the row's last page are fetched
 //               from out-of-range coordinates, which TMA fills with zeros.
 //   warp 1      TMEM owner (512 columns: S_A 0..127, S_B 128..255, O_A 256..383,
-//               O_B 384..511) and, on one lane, the MMA issuer.  Per key tile t:
-//               O_A += P_A V_{t-1}, O_B += P_B V_{t-1}, then S_A = Q_A K_t^T,
-//               S_B = Q_B K_t^T; S_X is rewritten only after the P V that read
-//               P_X (stored in S_X's columns) has completed, and the two tiles
-//               interleave so one tile's softmax overlaps the other's MMAs.
+//               O_B 384..511) and, on one lane, the MMA issuer.  Per key tile t
+//               it issues O_A += P_A V_{t-1}, S_A = Q_A K_t^T, O_B += P_B V_{t-1},
+//               S_B = Q_B K_t^T, so one tile's softmax runs while the tensor
+//               pipe works on the other tile.  S_X is rewritten only after the
+//               P V that read P_X (stored in S_X's columns) has completed.
 //   warps 2..5  softmax of tile A, warps 6..9 of tile B: one thread per score
-//               row (= TMEM lane).  Pass 1 reads the S row from TMEM for the
-//               row max (scale to log2 units, bottom-right causal mask); a lazy
-//               rescale touches O only when the max grows by more than 2^8;
-//               pass 2 re-reads S, exponentiates and writes P as packed
-//               bf16/fp16 back into the S columns, where the P V MMA reads it
-//               as its A operand.  Epilogue: O / l from TMEM to global memory.
+//               row (= TMEM lane).  The S row is read from TMEM once into
+//               registers (bottom-right causal mask, row max in log2 units),
+//               exponentiated and written back as packed bf16/fp16 P over the
+//               first 64 S columns, where the P V MMA reads it as its A
+//               operand; a lazy rescale touches O only when the running max
+//               grows by more than 2^8.  Epilogue: O / l from TMEM to global.
 // Every mbarrier wait is bounded; on a time-out the CTA records
 // BL_DEVERR_TIMEOUT, drains what it issued and frees its TMEM.
 // Roofline: tensor.  Algorithmic flops per request: 4 * Hq * D * (C*P + C(C+1)/2).
@@ -76,7 +76,7 @@ struct Args {
 
 struct Shared {
   uint64_t full_k[kStages], full_v[kStages], empty_k[kStages], empty_v[kStages];
-  uint64_t s_full[2], p_full[2], pv_done[2], q_full, mma_done;
+  uint64_t s_full[2], p_full[2], pv_done[2], q_full, mma_done, v_fixed;
   uint32_t tmem_base;
   int abort;
 };
@@ -116,6 +116,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool table_short = npages > a.bt_width;
   if (table_short) npages = a.bt_width;
   const int ntiles = (npages + kPPT - 1) / kPPT;
+  // Pool slots past the row length hold stale bytes (possibly NaN): P is 0 there
+  // but 0 * NaN is NaN, so those V rows of the last key tile are zeroed in
+  // shared memory before the last P V.
+  const int64_t last_k0 = (int64_t)(ntiles - 1) * kKT;
+  const int v_first_bad = len - last_k0 < kKT ? (int)(len - last_k0) : kKT;
+  const int v_last_real = min(npages * kBS - (ntiles - 1) * kKT, kKT);
+  const bool fix_v = ntiles > 0 && v_first_bad < v_last_real;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -133,6 +140,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(&sh->q_full, kRows);
     mbar_init(&sh->mma_done, 1);
+    mbar_init(&sh->v_fixed, 1);
     sh->abort = 0;
     fence_mbar_init();
   }
@@ -144,13 +152,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------ producer ------------------------------
+    int issued_k = 0, issued_v = 0;
     if (lane == 0) {
       if (table_short) raise_dev(a.err, BL_DEVERR_TABLE);
       prefetch_tensormap(&kmap);
       prefetch_tensormap(&vmap);
       const int64_t row = a.row_ids ? (int64_t)a.row_ids[b] : b;
       const int32_t* bt = a.block_tables + row * a.bt_stride;
-      int issued_k = 0, issued_v = 0;
       auto load = [&](const CUtensorMap* map, uint64_t* full, unsigned char* dst, int t) {
         int32_t ys[kPPT];
 #pragma unroll
@@ -188,6 +196,27 @@ __global__ void __launch_bounds__(kThreads, 1)
           ++issued_v;
         }
       }
+    }
+    if (fix_v) {
+      // the whole warp zeroes the stale V rows of the last tile, then releases
+      // the last P V
+      const int j = ntiles - 1, s = j & 1;
+      const bool got = __shfl_sync(0xffffffffu, issued_v, 0) == ntiles &&
+                       __all_sync(0xffffffffu, wait_or_abort(&sh->full_v[s], (j >> 1) & 1, sh, a.err));
+      if (got) {
+        unsigned char* vs = smem + kOffV + s * kTile;
+        const int nchunks = (v_last_real - v_first_bad) * 16;  // rows x (2 halves x 8 chunks)
+        for (int e = lane; e < nchunks; e += 32) {
+          const int row_k = v_first_bad + e / 16;
+          const int rem = e % 16;
+          *reinterpret_cast<uint4*>(vs + (rem >> 3) * kHalf + row_k * 128 + ((rem & 7) << 4)) = make_uint4(0, 0, 0, 0);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sh->v_fixed);
+      }
+    }
+    if (lane == 0) {
       // drain: every issued copy must land before the CTA can exit
       for (int s = 0; s < kStages; ++s) {
         if (s < issued_k) {
@@ -205,48 +234,55 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       const uint32_t idesc_s = umma_idesc_f16(kTileRows, kKT, BF16, false);
       const uint32_t idesc_o = umma_idesc_f16(kTileRows, kD, BF16, true);
-      bool ok = wait_or_abort(&sh->q_full, 0, sh, a.err);
-      if (ok) tc_fence_after();
-      auto issue_pv = [&](int j) -> bool {  // O_X += P_X V_j for both tiles
-        const int s = j & 1;
-        if (!wait_or_abort(&sh->full_v[s], (j >> 1) & 1, sh, a.err)) return false;
-        const uint32_t sv = smem_u32(smem + kOffV + s * kTile);
-        for (int x = 0; x < 2; ++x) {
-          if (!wait_or_abort(&sh->p_full[x], j & 1, sh, a.err)) return false;
-          tc_fence_after();
+      // O_X += P_X V_j (P_X in S_X's TMEM columns)
+      auto pv = [&](int x, int j) -> bool {
+        if (!wait_or_abort(&sh->p_full[x], j & 1, sh, a.err)) return false;
+        tc_fence_after();
+        const uint32_t sv = smem_u32(smem + kOffV + (j & 1) * kTile);
 #pragma unroll
-          for (int kk = 0; kk < kKT / 16; ++kk) {
-            const uint64_t db = umma_desc_sw128(sv + kk * 2048, kHalf, 1024);
-            tc_mma_ts(tmem + kColO + x * 128, tmem + kColS + x * 128 + kk * 8, db, idesc_o,
-                      (j > 0 || kk > 0) ? 1u : 0u);
-          }
-          tc_commit(&sh->pv_done[x]);
-        }
-        tc_commit(&sh->empty_v[s]);
+        for (int kk = 0; kk < kKT / 16; ++kk)
+          tc_mma_ts(tmem + kColO + x * 128, tmem + kColS + x * 128 + kk * 8,
+                    umma_desc_sw128(sv + kk * 2048, kHalf, 1024), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&sh->pv_done[x]);
         return true;
       };
-      for (int t = 0; t < ntiles && ok; ++t) {
-        if (t >= 1 && !(ok = issue_pv(t - 1))) break;
-        const int s = t & 1;
-        if (!(ok = wait_or_abort(&sh->full_k[s], (t >> 1) & 1, sh, a.err))) break;
-        const uint32_t sk = smem_u32(smem + kOffK + s * kTile);
-        for (int x = 0; x < 2; ++x) {
-          // S_X is rewritten only after the P V that read P_X from it is done
-          if (t >= 1 && !(ok = wait_or_abort(&sh->pv_done[x], (t - 1) & 1, sh, a.err))) break;
-          tc_fence_after();
-          const uint32_t sq = smem_u32(smem + kOffQ + x * kTile);
+      // S_X = Q_X K_t^T, once the P V that last read S_X's columns is done
+      auto qk = [&](int x, int t) -> bool {
+        if (t >= 1 && !wait_or_abort(&sh->pv_done[x], (t - 1) & 1, sh, a.err)) return false;
+        tc_fence_after();
+        const uint32_t sq = smem_u32(smem + kOffQ + x * kTile);
+        const uint32_t sk = smem_u32(smem + kOffK + (t & 1) * kTile);
 #pragma unroll
-          for (int ks = 0; ks < kD / 16; ++ks) {
-            const uint32_t off = (ks >> 2) * kHalf + (ks & 3) * 32;
-            tc_mma_ss(tmem + kColS + x * 128, umma_desc_sw128(sq + off, 16, 1024),
-                      umma_desc_sw128(sk + off, 16, 1024), idesc_s, ks > 0 ? 1u : 0u);
-          }
-          tc_commit(&sh->s_full[x]);
+        for (int ks = 0; ks < kD / 16; ++ks) {
+          const uint32_t off = (ks >> 2) * kHalf + (ks & 3) * 32;
+          tc_mma_ss(tmem + kColS + x * 128, umma_desc_sw128(sq + off, 16, 1024), umma_desc_sw128(sk + off, 16, 1024),
+                    idesc_s, ks > 0 ? 1u : 0u);
         }
-        if (!ok) break;
-        tc_commit(&sh->empty_k[s]);
+        tc_commit(&sh->s_full[x]);
+        return true;
+      };
+      // Issue order per key tile t >= 1:  PV_A(t-1), S_A(t), PV_B(t-1), S_B(t),
+      // so tile A's softmax of t runs while the tensor pipe works on tile B.
+      bool ok = wait_or_abort(&sh->q_full, 0, sh, a.err);
+      if (ok) tc_fence_after();
+      if (ok && ntiles > 0) {
+        ok = wait_or_abort(&sh->full_k[0], 0, sh, a.err) && qk(0, 0) && qk(1, 0);
+        if (ok) tc_commit(&sh->empty_k[0]);
       }
-      if (ok && ntiles > 0) ok = issue_pv(ntiles - 1);
+      for (int t = 1; t < ntiles && ok; ++t) {
+        const int j = t - 1;
+        ok = wait_or_abort(&sh->full_v[j & 1], (j >> 1) & 1, sh, a.err) && pv(0, j) &&
+             wait_or_abort(&sh->full_k[t & 1], (t >> 1) & 1, sh, a.err) && qk(0, t) && pv(1, j);
+        if (!ok) break;
+        tc_commit(&sh->empty_v[j & 1]);
+        if (!(ok = qk(1, t))) break;
+        tc_commit(&sh->empty_k[t & 1]);
+      }
+      if (ok && ntiles > 0) {
+        const int j = ntiles - 1;
+        ok = wait_or_abort(&sh->full_v[j & 1], (j >> 1) & 1, sh, a.err) &&
+             (!fix_v || wait_or_abort(&sh->v_fixed, 0, sh, a.err)) && pv(0, j) && pv(1, j);
+      }
       // every MMA issued here has finished before the CTA tears down
       tc_commit(&sh->mma_done);
       if (!mbar_wait(&sh->mma_done, 0)) raise_dev(a.err, BL_DEVERR_TIMEOUT);
@@ -290,79 +326,65 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       tc_fence_after();
       const int64_t k0 = (int64_t)t * kKT;
-      const bool masked = k0 + kKT - 1 > lim;
-      // pass 1: row max (S_X is complete, and so is the P V that last read it)
-      float mt = -INFINITY;
+      // the whole S row in registers: one TMEM read per tile
+      float v[kKT];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tc_ld32f(tl + sc + c * 32, v);
-        tc_wait_ld();
+      for (int c = 0; c < kKT / 32; ++c) tc_ld32f(tl + sc + c * 32, v + c * 32);
+      tc_wait_ld();
+      reg_fence<kKT>(v);
+      // bottom-right causal mask: keys past `lim` drop out (only tiles that
+      // cross the diagonal or the chunk end take this branch)
+      const int64_t lim_rel64 = lim - k0;
+      if (__any_sync(0xffffffffu, lim_rel64 < kKT - 1)) {
+        const int lim_rel = lim_rel64 < -1 ? -1 : (int)lim_rel64;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float y = (masked && k0 + c * 32 + j > lim) ? -INFINITY : v[j] * a.scale_log2;
-          mt = fmaxf(mt, y);
-        }
+        for (int j = 0; j < kKT; ++j) v[j] = j > lim_rel ? -INFINITY : v[j];
       }
+      // row max of the raw scores (the scale is positive), eight partial chains
+      float mp[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mp[i] = v[i];
+#pragma unroll
+      for (int j = 8; j < kKT; ++j) mp[j & 7] = fmaxf(mp[j & 7], v[j]);
+      const float mt = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
+                             fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7]))) * a.scale_log2;
       const float m_new = fmaxf(m_used, mt);
       const bool need = (t > 0) && (m_new > m_used + kRescaleThreshold);
       const float alpha = need ? fast_exp2(m_used - m_new) : 1.f;
       if (need || t == 0) m_used = m_new;
       const float ms = (m_used == -INFINITY) ? 0.f : m_used;
-      if (__any_sync(0xffffffffu, need)) {
+      // P = exp2(s * scale - m), packed two per column over S's first 64
+      // columns (S is already in registers)
+      float rp[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          float v[32];
-          tc_ld32f(tl + oc + c * 32, v);
-          tc_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] *= alpha;
-          tc_st32f(tl + oc + c * 32, v);
-        }
-      }
-      // pass 2: P = exp2(s - m) packed back over S (chunk c of P lands in
-      // columns already read: 16c .. 16c+15 <= 32c + 31)
-      float rs = 0.f;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tc_ld32f(tl + sc + c * 32, v);
-        tc_wait_ld();
+      for (int c = 0; c < kKT / 32; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          const int k = c * 32 + 2 * j;
-          const float y0 = (masked && k0 + k > lim) ? -INFINITY : v[2 * j] * a.scale_log2;
-          const float y1 = (masked && k0 + k + 1 > lim) ? -INFINITY : v[2 * j + 1] * a.scale_log2;
-          const float p0 = fast_exp2(y0 - ms), p1 = fast_exp2(y1 - ms);
-          rs += p0 + p1;
+          const float p0 = fast_exp2(fmaf(v[c * 32 + 2 * j], a.scale_log2, -ms));
+          const float p1 = fast_exp2(fmaf(v[c * 32 + 2 * j + 1], a.scale_log2, -ms));
+          rp[j & 3] += p0 + p1;
           pk[j] = pack2<T>(p0, p1);
         }
         tc_st16(tl + sc + c * 16, pk);
       }
-      tc_wait_st();
-      l = l * alpha + rs;
-      // Pool slots past the row length hold stale bytes (possibly NaN): P is 0
-      // there but 0 * NaN is NaN, so tile A's threads zero those V rows of the
-      // last key tile before P_A is published (P V of tile B is issued after A's).
-      if (x == 0 && t == ntiles - 1) {
-        const int first_bad = (int)(len - k0);
-        const int last_real = min(npages * kBS - t * kKT, kKT);
-        if (first_bad < last_real) {
-          const int s = t & 1;
-          ok = __all_sync(0xffffffffu, wait_or_abort(&sh->full_v[s], (t >> 1) & 1, sh, a.err));
-          if (!ok) break;
-          unsigned char* vs = smem + kOffV + s * kTile;
-          const int nchunks = (last_real - first_bad) * 16;  // rows x (2 halves x 8 chunks)
-          for (int e = tr; e < nchunks; e += kTileRows) {
-            const int row_k = first_bad + e / 16;
-            const int rem = e % 16;
-            *reinterpret_cast<uint4*>(vs + (rem >> 3) * kHalf + row_k * 128 + ((rem & 7) << 4)) =
-                make_uint4(0, 0, 0, 0);
-          }
-          fence_proxy_async_smem();
+      const float rs = (rp[0] + rp[1]) + (rp[2] + rp[3]);
+      // lazy rescale of O (the P V that last wrote O_X completed before S_X was
+      // issued); rare once the running max has settled
+      if (__any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float o[32];
+          tc_ld32f(tl + oc + c * 32, o);
+          tc_wait_ld();
+          reg_fence<32>(o);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) o[j] *= alpha;
+          tc_st32f(tl + oc + c * 32, o);
         }
       }
+      tc_wait_st();
+      l = l * alpha + rs;
       tc_fence_before();
       mbar_arrive(&sh->p_full[x]);
     }
@@ -378,6 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           float o[32];
           tc_ld32f(tl + oc + c * 32, o);
           tc_wait_ld();
+          reg_fence<32>(o);
           if (valid) {
 #pragma unroll
             for (int j = 0; j < 16; ++j)
