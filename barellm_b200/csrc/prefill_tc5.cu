@@ -7,18 +7,21 @@
 // G >= 2 both tiles cover the same tokens and need the same keys).  Every K/V
 // page is fetched once for 256 rows, which halves the K/V bytes per flop of a
 // 128-row tile; keys are consumed in tiles of 128 (8 pages).  Warp roles:
-//   warp 0      TMA producer: K and V pages of a key tile, each page two 64 x 16
-//               boxes with the 128-byte swizzle, into 2-stage K and V rings.  K
-//               runs a tile ahead of V (K slots free up after Q K^T, V slots
-//               only after P V).  Pages past the row's last page are fetched
-//               from out-of-range coordinates, which TMA fills with zeros.
-//   warp 1      TMEM owner (512 columns: S_A 0..127, S_B 128..255, O_A 256..383,
+//   warps 0..1  producers: K and V pages of a key tile into 2-stage K and V
+//               rings, 16-byte cp.async per thread written in the 128-byte
+//               swizzled layout the MMA reads (paged 4 KB pages stream about
+//               four times faster this way than as 2 KB TMA boxes).  Each
+//               thread's copies arrive on the stage's mbarrier when they land;
+//               V of tile t-1 goes out before K of tile t (P V comes first).
+//               Slots past the row length or the row's last page are written
+//               as zeros (src-size 0), so stale pool bytes never reach P V.
+//   warp 2      TMEM owner (512 columns: S_A 0..127, S_B 128..255, O_A 256..383,
 //               O_B 384..511) and, on one lane, the MMA issuer.  Per key tile t
 //               it issues O_A += P_A V_{t-1}, S_A = Q_A K_t^T, O_B += P_B V_{t-1},
 //               S_B = Q_B K_t^T, so one tile's softmax runs while the tensor
 //               pipe works on the other tile.  S_X is rewritten only after the
 //               P V that read P_X (stored in S_X's columns) has completed.
-//   warps 2..5  softmax of tile A, warps 6..9 of tile B: one thread per score
+//   warps 3..6  softmax of tile A, warps 7..10 of tile B: one thread per score
 //               row (= TMEM lane).  The S row is read from TMEM once into
 //               registers (bottom-right causal mask, row max in log2 units),
 //               exponentiated and written back as packed bf16/fp16 P over the
@@ -42,10 +45,12 @@ constexpr int kPPT = kKT / kBS;          // 8 pages per tile
 constexpr int kTileRows = 128;           // rows per MMA tile (M)
 constexpr int kRows = 2 * kTileRows;     // score rows per CTA
 constexpr int kStages = 2;
-constexpr int kThreads = 320;            // producer, MMA, 2 x 4 softmax warps
+constexpr int kProducers = 64;           // threads of warps 0..1
+constexpr int kMmaWarp = 2;
+constexpr int kSoftmaxWarp0 = 3;
+constexpr int kThreads = 352;            // 2 producer warps, MMA warp, 2 x 4 softmax warps
 constexpr int kHalf = 128 * 128;         // 16 KB: 128 rows x 128 B (64 elements of D or K)
 constexpr int kTile = 2 * kHalf;         // 32 KB
-constexpr int kPageHalf = kBS * 128;     // 2 KB: 16 rows x 128 B
 constexpr int kOffQ = 0;                        // + X * kTile
 constexpr int kOffK = 2 * kTile;                // + s * kTile
 constexpr int kOffV = kOffK + kStages * kTile;  // + s * kTile
@@ -67,16 +72,17 @@ struct Args {
   int64_t bt_stride;
   int32_t bt_width;
   const int32_t* row_ids;
+  const uint16_t* k_pool;
+  const uint16_t* v_pool;
   int32_t hkv, g, bq;  // bq = query tokens per CTA = kRows / g
   int64_t num_blocks, layer_row0, max_q;
-  int32_t rows_total;  // rows of the pool tensor map: an out-of-range coordinate
   float scale_log2;
   int32_t* err;
 };
 
 struct Shared {
   uint64_t full_k[kStages], full_v[kStages], empty_k[kStages], empty_v[kStages];
-  uint64_t s_full[2], p_full[2], pv_done[2], q_full, mma_done, v_fixed;
+  uint64_t s_full[2], p_full[2], pv_done[2], q_full, mma_done;
   uint32_t tmem_base;
   int abort;
 };
@@ -91,7 +97,7 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, Sh
 
 template <bool BF16>
 __global__ void __launch_bounds__(kThreads, 1)
-    prefill_tc5_kernel(const Args a, const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap) {
+    prefill_tc5_kernel(const Args a) {
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
@@ -116,20 +122,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool table_short = npages > a.bt_width;
   if (table_short) npages = a.bt_width;
   const int ntiles = (npages + kPPT - 1) / kPPT;
-  // Pool slots past the row length hold stale bytes (possibly NaN): P is 0 there
-  // but 0 * NaN is NaN, so those V rows of the last key tile are zeroed in
-  // shared memory before the last P V.
-  const int64_t last_k0 = (int64_t)(ntiles - 1) * kKT;
-  const int v_first_bad = len - last_k0 < kKT ? (int)(len - last_k0) : kKT;
-  const int v_last_real = min(npages * kBS - (ntiles - 1) * kKT, kKT);
-  const bool fix_v = ntiles > 0 && v_first_bad < v_last_real;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&sh->full_k[s], 1);
-      mbar_init(&sh->full_v[s], 1);
+      mbar_init(&sh->full_k[s], kProducers);
+      mbar_init(&sh->full_v[s], kProducers);
       mbar_init(&sh->empty_k[s], 1);
       mbar_init(&sh->empty_v[s], 1);
     }
@@ -140,109 +139,89 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(&sh->q_full, kRows);
     mbar_init(&sh->mma_done, 1);
-    mbar_init(&sh->v_fixed, 1);
     sh->abort = 0;
     fence_mbar_init();
   }
-  if (warp == 1) tc_alloc(&sh->tmem_base, kTmemCols);
+  if (warp == kMmaWarp) tc_alloc(&sh->tmem_base, kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sh->tmem_base;
 
-  if (warp == 0) {
-    // ------------------------------ producer ------------------------------
-    int issued_k = 0, issued_v = 0;
-    if (lane == 0) {
-      if (table_short) raise_dev(a.err, BL_DEVERR_TABLE);
-      prefetch_tensormap(&kmap);
-      prefetch_tensormap(&vmap);
-      const int64_t row = a.row_ids ? (int64_t)a.row_ids[b] : b;
-      const int32_t* bt = a.block_tables + row * a.bt_stride;
-      auto load = [&](const CUtensorMap* map, uint64_t* full, unsigned char* dst, int t) {
-        int32_t ys[kPPT];
-#pragma unroll
-        for (int p = 0; p < kPPT; ++p) {
-          const int lb = t * kPPT + p;
-          if (lb < npages) {
-            int64_t phys = bt[lb];
-            if (phys < 0 || phys >= a.num_blocks) {
-              raise_dev(a.err, BL_DEVERR_BLOCK_ID);
-              phys = 0;
-            }
-            ys[p] = (int32_t)(a.layer_row0 + (phys * a.hkv + h) * kBS);
-          } else {
-            ys[p] = a.rows_total;  // fully out of range: TMA writes zeros
+  if (warp < kMmaWarp) {
+    // ------------------------------ producers ------------------------------
+    // Thread pt copies 16-byte chunk (pt & 15) of rows r0, r0+4, r0+8, r0+12
+    // (r0 = pt >> 4) of each of the tile's 8 pages: 32 copies per tile.
+    const int pt = threadIdx.x;
+    if (pt == 0 && table_short) raise_dev(a.err, BL_DEVERR_TABLE);
+    const int64_t brow = a.row_ids ? (int64_t)a.row_ids[b] : b;
+    const int32_t* bt = a.block_tables + brow * a.bt_stride;
+    const int cc = pt & 15, r0 = pt >> 4;
+    const uint32_t dst_col = (uint32_t)(cc >> 3) * kHalf;
+    auto load = [&](const uint16_t* pool, unsigned char* stage, uint64_t* full, int t) {
+#pragma unroll 2
+      for (int p = 0; p < kPPT; ++p) {
+        const int lb = t * kPPT + p;
+        int64_t phys = -1;
+        if (lb < npages) {
+          phys = bt[lb];
+          if (phys < 0 || phys >= a.num_blocks) {
+            raise_dev(a.err, BL_DEVERR_BLOCK_ID);
+            phys = -1;
           }
         }
-        mbar_arrive_expect_tx(full, kTile);
+        const uint16_t* src = pool + ((a.layer_row0 + ((phys < 0 ? 0 : phys) * a.hkv + h) * kBS) * kD + cc * 8);
+        const int64_t key0 = (int64_t)lb * kBS;
 #pragma unroll
-        for (int p = 0; p < kPPT; ++p) {
-          tma_load_2d(dst + p * kPageHalf, map, full, 0, ys[p]);
-          tma_load_2d(dst + kHalf + p * kPageHalf, map, full, 64, ys[p]);
-        }
-      };
-      for (int t = 0; t <= ntiles; ++t) {
-        if (t < ntiles) {
-          const int s = t & 1;
-          if (!wait_or_abort(&sh->empty_k[s], ((t >> 1) & 1) ^ 1, sh, a.err)) break;
-          load(&kmap, &sh->full_k[s], smem + kOffK + s * kTile, t);
-          ++issued_k;
-        }
-        if (t >= 1) {
-          const int j = t - 1, s = j & 1;
-          if (!wait_or_abort(&sh->empty_v[s], ((j >> 1) & 1) ^ 1, sh, a.err)) break;
-          load(&vmap, &sh->full_v[s], smem + kOffV + s * kTile, j);
-          ++issued_v;
+        for (int j = 0; j < 4; ++j) {
+          const int r = r0 + 4 * j;
+          const uint32_t bytes = (phys >= 0 && key0 + r < len) ? 16u : 0u;
+          const uint32_t dst = smem_u32(stage + dst_col + (p * kBS + r) * 128 + (((cc & 7) ^ (r & 7)) << 4));
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src + r * kD), "r"(bytes)
+                       : "memory");
         }
       }
-    }
-    if (fix_v) {
-      // the whole warp zeroes the stale V rows of the last tile, then releases
-      // the last P V
-      const int j = ntiles - 1, s = j & 1;
-      const bool got = __shfl_sync(0xffffffffu, issued_v, 0) == ntiles &&
-                       __all_sync(0xffffffffu, wait_or_abort(&sh->full_v[s], (j >> 1) & 1, sh, a.err));
-      if (got) {
-        unsigned char* vs = smem + kOffV + s * kTile;
-        const int nchunks = (v_last_real - v_first_bad) * 16;  // rows x (2 halves x 8 chunks)
-        for (int e = lane; e < nchunks; e += 32) {
-          const int row_k = v_first_bad + e / 16;
-          const int rem = e % 16;
-          *reinterpret_cast<uint4*>(vs + (rem >> 3) * kHalf + row_k * 128 + ((rem & 7) << 4)) = make_uint4(0, 0, 0, 0);
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sh->v_fixed);
+      asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(full)) : "memory");
+    };
+    for (int t = 0; t <= ntiles; ++t) {
+      if (t >= 1) {
+        const int j = t - 1, s = j & 1;
+        if (!wait_or_abort(&sh->empty_v[s], ((j >> 1) & 1) ^ 1, sh, a.err)) break;
+        load(a.v_pool, smem + kOffV + s * kTile, &sh->full_v[s], j);
+      }
+      if (t < ntiles) {
+        const int s = t & 1;
+        if (!wait_or_abort(&sh->empty_k[s], ((t >> 1) & 1) ^ 1, sh, a.err)) break;
+        load(a.k_pool, smem + kOffK + s * kTile, &sh->full_k[s], t);
       }
     }
-    if (lane == 0) {
-      // drain: every issued copy must land before the CTA can exit
-      for (int s = 0; s < kStages; ++s) {
-        if (s < issued_k) {
-          const int last = s + ((issued_k - 1 - s) / kStages) * kStages;
-          if (!mbar_wait(&sh->full_k[s], (last >> 1) & 1)) raise_dev(a.err, BL_DEVERR_TIMEOUT);
-        }
-        if (s < issued_v) {
-          const int last = s + ((issued_v - 1 - s) / kStages) * kStages;
-          if (!mbar_wait(&sh->full_v[s], (last >> 1) & 1)) raise_dev(a.err, BL_DEVERR_TIMEOUT);
-        }
-      }
-    }
-  } else if (warp == 1) {
+    // every copy this thread issued lands before the CTA can exit
+    asm volatile("cp.async.wait_all;" ::: "memory");
+  } else if (warp == kMmaWarp) {
     // ------------------------------ MMA issuer ------------------------------
     if (lane == 0) {
       const uint32_t idesc_s = umma_idesc_f16(kTileRows, kKT, BF16, false);
       const uint32_t idesc_o = umma_idesc_f16(kTileRows, kD, BF16, true);
       // O_X += P_X V_j (P_X in S_X's TMEM columns)
+      // Shared-memory descriptors are built once; an MMA's operand address is
+      // the base descriptor plus its (16-byte unit) offset, so the single
+      // issuing thread spends a few instructions per MMA (a 128 x 128 x 16 step
+      // takes 64 cycles on the tensor pipe, less than rebuilding descriptors).
+      const uint64_t dq0 = umma_desc_sw128(smem_u32(smem + kOffQ), 16, 1024);
+      const uint64_t dq1 = umma_desc_sw128(smem_u32(smem + kOffQ + kTile), 16, 1024);
+      const uint64_t dk0 = umma_desc_sw128(smem_u32(smem + kOffK), 16, 1024);
+      const uint64_t dk1 = umma_desc_sw128(smem_u32(smem + kOffK + kTile), 16, 1024);
+      const uint64_t dv0 = umma_desc_sw128(smem_u32(smem + kOffV), kHalf, 1024);
+      const uint64_t dv1 = umma_desc_sw128(smem_u32(smem + kOffV + kTile), kHalf, 1024);
+      // O_X += P_X V_j (P_X in S_X's TMEM columns)
       auto pv = [&](int x, int j) -> bool {
         if (!wait_or_abort(&sh->p_full[x], j & 1, sh, a.err)) return false;
         tc_fence_after();
-        const uint32_t sv = smem_u32(smem + kOffV + (j & 1) * kTile);
+        const uint64_t dv = (j & 1) ? dv1 : dv0;
+        const uint32_t d = tmem + kColO + x * 128, pa = tmem + kColS + x * 128;
+        tc_mma_ts(d, pa, dv, idesc_o, j > 0 ? 1u : 0u);
 #pragma unroll
-        for (int kk = 0; kk < kKT / 16; ++kk)
-          tc_mma_ts(tmem + kColO + x * 128, tmem + kColS + x * 128 + kk * 8,
-                    umma_desc_sw128(sv + kk * 2048, kHalf, 1024), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 1; kk < kKT / 16; ++kk) tc_mma_ts(d, pa + kk * 8, dv + ((kk * 2048) >> 4), idesc_o, 1u);
         tc_commit(&sh->pv_done[x]);
         return true;
       };
@@ -250,15 +229,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto qk = [&](int x, int t) -> bool {
         if (t >= 1 && !wait_or_abort(&sh->pv_done[x], (t - 1) & 1, sh, a.err)) return false;
         tc_fence_after();
-        const uint32_t sq = smem_u32(smem + kOffQ + x * kTile);
-        const uint32_t sk = smem_u32(smem + kOffK + (t & 1) * kTile);
+        const uint64_t dq = x ? dq1 : dq0, dk = (t & 1) ? dk1 : dk0;
+        const uint32_t d = tmem + kColS + x * 128;
 #pragma unroll
         for (int ks = 0; ks < kD / 16; ++ks) {
-          const uint32_t off = (ks >> 2) * kHalf + (ks & 3) * 32;
-          tc_mma_ss(tmem + kColS + x * 128, umma_desc_sw128(sq + off, 16, 1024), umma_desc_sw128(sk + off, 16, 1024),
-                    idesc_s, ks > 0 ? 1u : 0u);
+          const uint32_t off = ((ks >> 2) * kHalf + (ks & 3) * 32) >> 4;
+          tc_mma_ss(d, dq + off, dk + off, idesc_s, ks > 0 ? 1u : 0u);
         }
         tc_commit(&sh->s_full[x]);
+        return true;
+      };
+      // A stage's copies were written by other threads through the generic
+      // proxy; after its mbarrier completes, a proxy fence orders them before
+      // the tensor core's reads.
+      auto landed = [&](uint64_t* full, uint32_t parity) -> bool {
+        if (!wait_or_abort(full, parity, sh, a.err)) return false;
+        fence_proxy_async_smem();
         return true;
       };
       // Issue order per key tile t >= 1:  PV_A(t-1), S_A(t), PV_B(t-1), S_B(t),
@@ -266,13 +252,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = wait_or_abort(&sh->q_full, 0, sh, a.err);
       if (ok) tc_fence_after();
       if (ok && ntiles > 0) {
-        ok = wait_or_abort(&sh->full_k[0], 0, sh, a.err) && qk(0, 0) && qk(1, 0);
+        ok = landed(&sh->full_k[0], 0) && qk(0, 0) && qk(1, 0);
         if (ok) tc_commit(&sh->empty_k[0]);
       }
       for (int t = 1; t < ntiles && ok; ++t) {
         const int j = t - 1;
-        ok = wait_or_abort(&sh->full_v[j & 1], (j >> 1) & 1, sh, a.err) && pv(0, j) &&
-             wait_or_abort(&sh->full_k[t & 1], (t >> 1) & 1, sh, a.err) && qk(0, t) && pv(1, j);
+        ok = landed(&sh->full_v[j & 1], (j >> 1) & 1) && pv(0, j) && landed(&sh->full_k[t & 1], (t >> 1) & 1) &&
+             qk(0, t) && pv(1, j);
         if (!ok) break;
         tc_commit(&sh->empty_v[j & 1]);
         if (!(ok = qk(1, t))) break;
@@ -280,8 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (ok && ntiles > 0) {
         const int j = ntiles - 1;
-        ok = wait_or_abort(&sh->full_v[j & 1], (j >> 1) & 1, sh, a.err) &&
-             (!fix_v || wait_or_abort(&sh->v_fixed, 0, sh, a.err)) && pv(0, j) && pv(1, j);
+        ok = landed(&sh->full_v[j & 1], (j >> 1) & 1) && pv(0, j) && pv(1, j);
       }
       // every MMA issued here has finished before the CTA tears down
       tc_commit(&sh->mma_done);
@@ -289,7 +274,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------ softmax ------------------------------
-    const int x = (warp - 2) >> 2;        // tile: 0 = A, 1 = B
+    const int x = (warp - kSoftmaxWarp0) >> 2;  // tile: 0 = A, 1 = B
     const int grp = warp & 3;             // TMEM lane group
     const int tr = 32 * grp + lane;       // row within the tile == TMEM lane
     const int r = x * kTileRows + tr;     // row within the CTA
@@ -413,7 +398,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tc_dealloc(tmem, kTmemCols);
   }
@@ -432,10 +417,6 @@ int launch(const bl_prefill_args& a, cudaStream_t s) {
     }
     attr_done = true;
   }
-  const uint64_t rows = (uint64_t)a.kv.num_layers * a.kv.num_blocks * a.kv.num_kv_heads * kBS;
-  CUtensorMap kmap, vmap;
-  if (!get_pool_tmap(a.kv.k_pool, rows, a.kv.dtype, &kmap) || !get_pool_tmap(a.kv.v_pool, rows, a.kv.dtype, &vmap))
-    return BL_ERR_LAUNCH;
   Args k;
   k.q = a.q;
   k.q_sb = a.q_stride_b;
@@ -457,12 +438,13 @@ int launch(const bl_prefill_args& a, cudaStream_t s) {
   k.num_blocks = a.kv.num_blocks;
   k.layer_row0 = (int64_t)a.kv.layer * a.kv.num_blocks * a.kv.num_kv_heads * kBS;
   k.max_q = a.max_q_len;
-  k.rows_total = (int32_t)rows;
+  k.k_pool = static_cast<const uint16_t*>(a.kv.k_pool);
+  k.v_pool = static_cast<const uint16_t*>(a.kv.v_pool);
   k.scale_log2 = a.scale * kLog2e;
   k.err = a.err;
   const int64_t tiles = (a.max_q_len + k.bq - 1) / k.bq;
   dim3 grid((unsigned)tiles, (unsigned)a.kv.num_kv_heads, (unsigned)a.batch);
-  prefill_tc5_kernel<BF16><<<grid, kThreads, smem_bytes(), s>>>(k, kmap, vmap);
+  prefill_tc5_kernel<BF16><<<grid, kThreads, smem_bytes(), s>>>(k);
   BL_CHECK_LAUNCH("prefill_tc5_kernel");
   return BL_OK;
 }
@@ -470,8 +452,6 @@ int launch(const bl_prefill_args& a, cudaStream_t s) {
 }  // namespace
 
 int prefill_tc5_launch(const bl_prefill_args& a, cudaStream_t s) {
-  const uint64_t rows = (uint64_t)a.kv.num_layers * a.kv.num_blocks * a.kv.num_kv_heads * kBS;
-  BL_CHECK_ARG(rows + kBS <= (uint64_t)INT32_MAX, "bl_paged_prefill: pool has more than 2^31 rows");
   BL_CHECK_ARG(((uintptr_t)a.kv.k_pool & 15) == 0 && ((uintptr_t)a.kv.v_pool & 15) == 0,
                "bl_paged_prefill: pools must be 16-byte aligned");
   BL_CHECK_ARG(((uintptr_t)a.q & 3) == 0 && ((uintptr_t)a.out & 3) == 0 && a.q_stride_b % 2 == 0 &&
