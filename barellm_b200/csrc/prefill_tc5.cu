@@ -44,17 +44,18 @@ constexpr int kKT = 128;                 // keys per tile
 constexpr int kPPT = kKT / kBS;          // 8 pages per tile
 constexpr int kTileRows = 128;           // rows per MMA tile (M)
 constexpr int kRows = 2 * kTileRows;     // score rows per CTA
-constexpr int kStages = 2;
-constexpr int kProducers = 64;           // threads of warps 0..1
-constexpr int kMmaWarp = 2;
-constexpr int kSoftmaxWarp0 = 3;
-constexpr int kThreads = 352;            // 2 producer warps, MMA warp, 2 x 4 softmax warps
+constexpr int kKStages = 3;             // K: 3 x 32 KB (K of tile t is read after P V of t-1)
+constexpr int kVStages = 2;
+constexpr int kVProducers = 64;          // threads of warps 1..2 (V by cp.async); warp 0 issues K by TMA
+constexpr int kMmaWarp = 3;
+constexpr int kSoftmaxWarp0 = 4;
+constexpr int kThreads = 384;            // 3 producer warps, MMA warp, 2 x 4 softmax warps
 constexpr int kHalf = 128 * 128;         // 16 KB: 128 rows x 128 B (64 elements of D or K)
 constexpr int kTile = 2 * kHalf;         // 32 KB
 constexpr int kOffQ = 0;                        // + X * kTile
 constexpr int kOffK = 2 * kTile;                // + s * kTile
-constexpr int kOffV = kOffK + kStages * kTile;  // + s * kTile
-constexpr int kSmemData = kOffV + kStages * kTile;  // 192 KB
+constexpr int kOffV = kOffK + kKStages * kTile;  // + s * kTile
+constexpr int kSmemData = kOffV + kVStages * kTile;  // 224 KB
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0;                   // + X * 128 (P_X aliases the first 64 columns)
 constexpr uint32_t kColO = 256;                 // + X * 128
@@ -74,6 +75,8 @@ struct Args {
   const int32_t* row_ids;
   const uint16_t* k_pool;
   const uint16_t* v_pool;
+  int32_t q_vec16;  // q rows start on 16-byte boundaries (pointer and strides)
+  int32_t rows_total;  // rows of the K tensor map: an out-of-range row coordinate
   int32_t hkv, g, bq;  // bq = query tokens per CTA = kRows / g
   int64_t num_blocks, layer_row0, max_q;
   float scale_log2;
@@ -81,7 +84,7 @@ struct Args {
 };
 
 struct Shared {
-  uint64_t full_k[kStages], full_v[kStages], empty_k[kStages], empty_v[kStages];
+  uint64_t full_k[kKStages], full_v[kVStages], empty_k[kKStages], empty_v[kVStages];
   uint64_t s_full[2], p_full[2], pv_done[2], q_full, mma_done;
   uint32_t tmem_base;
   int abort;
@@ -97,7 +100,7 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, Sh
 
 template <bool BF16>
 __global__ void __launch_bounds__(kThreads, 1)
-    prefill_tc5_kernel(const Args a) {
+    prefill_tc5_kernel(const Args a, const __grid_constant__ CUtensorMap kmap) {
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
@@ -126,10 +129,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&sh->full_k[s], kProducers);
-      mbar_init(&sh->full_v[s], kProducers);
+    for (int s = 0; s < kKStages; ++s) {
+      mbar_init(&sh->full_k[s], 1);
       mbar_init(&sh->empty_k[s], 1);
+    }
+    for (int s = 0; s < kVStages; ++s) {
+      mbar_init(&sh->full_v[s], kVProducers);
       mbar_init(&sh->empty_v[s], 1);
     }
     for (int x = 0; x < 2; ++x) {
@@ -150,49 +155,74 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp < kMmaWarp) {
     // ------------------------------ producers ------------------------------
-    // Thread pt copies 16-byte chunk (pt & 15) of rows r0, r0+4, r0+8, r0+12
-    // (r0 = pt >> 4) of each of the tile's 8 pages: 32 copies per tile.
-    const int pt = threadIdx.x;
-    if (pt == 0 && table_short) raise_dev(a.err, BL_DEVERR_TABLE);
     const int64_t brow = a.row_ids ? (int64_t)a.row_ids[b] : b;
     const int32_t* bt = a.block_tables + brow * a.bt_stride;
-    const int cc = pt & 15, r0 = pt >> 4;
-    const uint32_t dst_col = (uint32_t)(cc >> 3) * kHalf;
-    auto load = [&](const uint16_t* pool, unsigned char* stage, uint64_t* full, int t) {
-#pragma unroll 2
-      for (int p = 0; p < kPPT; ++p) {
-        const int lb = t * kPPT + p;
-        int64_t phys = -1;
-        if (lb < npages) {
-          phys = bt[lb];
-          if (phys < 0 || phys >= a.num_blocks) {
-            raise_dev(a.err, BL_DEVERR_BLOCK_ID);
-            phys = -1;
+    if (warp == 0) {
+      // K: one TMA per page half (64 x 16 box, 128-byte swizzle); pages past
+      // the row's last page come from an out-of-range row, which TMA fills
+      // with zeros (stale rows inside the last page are masked out of S).
+      if (lane == 0) {
+        if (table_short) raise_dev(a.err, BL_DEVERR_TABLE);
+        prefetch_tensormap(&kmap);
+        for (int t = 0; t < ntiles; ++t) {
+          const int s = t % kKStages;
+          if (!wait_or_abort(&sh->empty_k[s], ((t / kKStages) & 1) ^ 1, sh, a.err)) break;
+          unsigned char* dst = smem + kOffK + s * kTile;
+          mbar_arrive_expect_tx(&sh->full_k[s], kTile);
+#pragma unroll 1
+          for (int p = 0; p < kPPT; ++p) {
+            const int lb = t * kPPT + p;
+            int32_t y = a.rows_total;
+            if (lb < npages) {
+              const int64_t phys = bt[lb];
+              if (phys < 0 || phys >= a.num_blocks)
+                raise_dev(a.err, BL_DEVERR_BLOCK_ID);
+              else
+                y = (int32_t)(a.layer_row0 + (phys * a.hkv + h) * kBS);
+            }
+            tma_load_2d(dst + p * kBS * 128, &kmap, &sh->full_k[s], 0, y);
+            tma_load_2d(dst + kHalf + p * kBS * 128, &kmap, &sh->full_k[s], 64, y);
           }
         }
-        const uint16_t* src = pool + ((a.layer_row0 + ((phys < 0 ? 0 : phys) * a.hkv + h) * kBS) * kD + cc * 8);
-        const int64_t key0 = (int64_t)lb * kBS;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int r = r0 + 4 * j;
-          const uint32_t bytes = (phys >= 0 && key0 + r < len) ? 16u : 0u;
-          const uint32_t dst = smem_u32(stage + dst_col + (p * kBS + r) * 128 + (((cc & 7) ^ (r & 7)) << 4));
-          asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src + r * kD), "r"(bytes)
-                       : "memory");
+        // drain: the K copies in flight land before the CTA can exit
+        const int issued = ntiles;
+        for (int s = 0; s < kKStages && s < issued; ++s) {
+          const int last = s + ((issued - 1 - s) / kKStages) * kKStages;
+          if (!mbar_wait(&sh->full_k[s], (last / kKStages) & 1)) raise_dev(a.err, BL_DEVERR_TIMEOUT);
         }
       }
-      asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(full)) : "memory");
-    };
-    for (int t = 0; t <= ntiles; ++t) {
-      if (t >= 1) {
-        const int j = t - 1, s = j & 1;
+    } else {
+      // V: 8 pages x 16 rows x 16 chunks of 16 bytes per tile; thread vt copies
+      // chunks vt, vt + 64, ... (always chunk vt & 15 of a row); slots past the
+      // row length are zero-filled (src-size 0) so stale pool bytes never
+      // reach P V.  Lanes 0..7 look up the tile's pages, the others shuffle.
+      const int vt = threadIdx.x - 32;
+      const int cc = vt & 15;
+      const uint32_t dst_col = (uint32_t)(cc >> 3) * kHalf;
+      for (int j = 0; j < ntiles; ++j) {
+        const int s = j & 1;
         if (!wait_or_abort(&sh->empty_v[s], ((j >> 1) & 1) ^ 1, sh, a.err)) break;
-        load(a.v_pool, smem + kOffV + s * kTile, &sh->full_v[s], j);
-      }
-      if (t < ntiles) {
-        const int s = t & 1;
-        if (!wait_or_abort(&sh->empty_k[s], ((t >> 1) & 1) ^ 1, sh, a.err)) break;
-        load(a.k_pool, smem + kOffK + s * kTile, &sh->full_k[s], t);
+        unsigned char* stage = smem + kOffV + s * kTile;
+        int phys_l = -1;
+        if (lane < kPPT) {
+          const int lb = j * kPPT + lane;
+          if (lb < npages) {
+            const int64_t ph = bt[lb];
+            if (ph >= 0 && ph < a.num_blocks) phys_l = (int)ph;
+          }
+        }
+        const int64_t key_t = (int64_t)j * kKT;
+#pragma unroll 4
+        for (int e = vt; e < kPPT * kBS * 16; e += kVProducers) {
+          const int p = e >> 8, r = (e >> 4) & 15;
+          const int phys = __shfl_sync(0xffffffffu, phys_l, p);
+          const uint32_t bytes = (phys >= 0 && key_t + p * kBS + r < len) ? 16u : 0u;
+          const uint16_t* src =
+              a.v_pool + ((a.layer_row0 + ((int64_t)(phys < 0 ? 0 : phys) * a.hkv + h) * kBS + r) * kD + cc * 8);
+          const uint32_t dst = smem_u32(stage + dst_col + (p * kBS + r) * 128 + (((cc & 7) ^ (r & 7)) << 4));
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+        }
+        asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&sh->full_v[s])) : "memory");
       }
     }
     // every copy this thread issued lands before the CTA can exit
@@ -210,7 +240,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t dq0 = umma_desc_sw128(smem_u32(smem + kOffQ), 16, 1024);
       const uint64_t dq1 = umma_desc_sw128(smem_u32(smem + kOffQ + kTile), 16, 1024);
       const uint64_t dk0 = umma_desc_sw128(smem_u32(smem + kOffK), 16, 1024);
-      const uint64_t dk1 = umma_desc_sw128(smem_u32(smem + kOffK + kTile), 16, 1024);
+      const uint64_t dk_stride = (uint64_t)(kTile >> 4);  // one K stage, in 16-byte units
       const uint64_t dv0 = umma_desc_sw128(smem_u32(smem + kOffV), kHalf, 1024);
       const uint64_t dv1 = umma_desc_sw128(smem_u32(smem + kOffV + kTile), kHalf, 1024);
       // O_X += P_X V_j (P_X in S_X's TMEM columns)
@@ -229,7 +259,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto qk = [&](int x, int t) -> bool {
         if (t >= 1 && !wait_or_abort(&sh->pv_done[x], (t - 1) & 1, sh, a.err)) return false;
         tc_fence_after();
-        const uint64_t dq = x ? dq1 : dq0, dk = (t & 1) ? dk1 : dk0;
+        const uint64_t dq = x ? dq1 : dq0, dk = dk0 + (uint64_t)(t % kKStages) * dk_stride;
         const uint32_t d = tmem + kColS + x * 128;
 #pragma unroll
         for (int ks = 0; ks < kD / 16; ++ks) {
@@ -257,12 +287,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       for (int t = 1; t < ntiles && ok; ++t) {
         const int j = t - 1;
-        ok = landed(&sh->full_v[j & 1], (j >> 1) & 1) && pv(0, j) && landed(&sh->full_k[t & 1], (t >> 1) & 1) &&
-             qk(0, t) && pv(1, j);
+        ok = landed(&sh->full_v[j & 1], (j >> 1) & 1) && pv(0, j) &&
+             landed(&sh->full_k[t % kKStages], (t / kKStages) & 1) && qk(0, t) && pv(1, j);
         if (!ok) break;
         tc_commit(&sh->empty_v[j & 1]);
         if (!(ok = qk(1, t))) break;
-        tc_commit(&sh->empty_k[t & 1]);
+        tc_commit(&sh->empty_k[t % kKStages]);
       }
       if (ok && ntiles > 0) {
         const int j = ntiles - 1;
@@ -286,8 +316,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool valid = qi < nq;
     const int hq = h * a.g + hd;
     const int64_t lim = prefix + qi;  // inclusive key limit
-    // Q row -> shared memory (K-major, 128-byte swizzle)
-    {
+    // Q rows -> shared memory (K-major, 128-byte swizzle).  With 16-byte
+    // aligned rows the 256 softmax threads copy 16-byte chunks (a warp reads
+    // two whole 256-byte rows at a time); rows past the chunk end are zeros.
+    if (a.q_vec16) {
+      const int i = (warp - kSoftmaxWarp0) * 32 + lane;  // 0..255
+      const int qc = i & 15;
+#pragma unroll 4
+      for (int k = 0; k < 16; ++k) {
+        const int row = (i >> 4) + 16 * k;
+        const int rhd = row / a.bq, rtok = row - rhd * a.bq;
+        const int64_t rqi = q0 + rtok;
+        const bool rvalid = rqi < nq;
+        const T* src = reinterpret_cast<const T*>(a.q) + b * a.q_sb + (qo + (rvalid ? rqi : 0)) * a.q_st +
+                       (int64_t)(h * a.g + rhd) * a.q_sh + qc * 8;
+        const int rt = row & (kTileRows - 1);
+        const uint32_t dst = smem_u32(smem + kOffQ + (row >> 7) * kTile + (qc >> 3) * kHalf + rt * 128 +
+                                      (((qc & 7) ^ (rt & 7)) << 4));
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(rvalid ? 16u : 0u)
+                     : "memory");
+      }
+      asm volatile("cp.async.wait_all;" ::: "memory");
+    } else {
       const T* qrow = reinterpret_cast<const T*>(a.q) + b * a.q_sb + (qo + (valid ? qi : 0)) * a.q_st +
                       (int64_t)hq * a.q_sh;
       unsigned char* qs = smem + kOffQ + x * kTile + tr * 128;
@@ -438,13 +488,18 @@ int launch(const bl_prefill_args& a, cudaStream_t s) {
   k.num_blocks = a.kv.num_blocks;
   k.layer_row0 = (int64_t)a.kv.layer * a.kv.num_blocks * a.kv.num_kv_heads * kBS;
   k.max_q = a.max_q_len;
+  const uint64_t rows = (uint64_t)a.kv.num_layers * a.kv.num_blocks * a.kv.num_kv_heads * kBS;
+  CUtensorMap kmap;
+  if (!get_pool_tmap(a.kv.k_pool, rows, a.kv.dtype, &kmap)) return BL_ERR_LAUNCH;
+  k.rows_total = (int32_t)rows;
+  k.q_vec16 = ((uintptr_t)a.q % 16 == 0) && a.q_stride_b % 8 == 0 && a.q_stride_t % 8 == 0 && a.q_stride_h % 8 == 0;
   k.k_pool = static_cast<const uint16_t*>(a.kv.k_pool);
   k.v_pool = static_cast<const uint16_t*>(a.kv.v_pool);
   k.scale_log2 = a.scale * kLog2e;
   k.err = a.err;
   const int64_t tiles = (a.max_q_len + k.bq - 1) / k.bq;
   dim3 grid((unsigned)tiles, (unsigned)a.kv.num_kv_heads, (unsigned)a.batch);
-  prefill_tc5_kernel<BF16><<<grid, kThreads, smem_bytes(), s>>>(k);
+  prefill_tc5_kernel<BF16><<<grid, kThreads, smem_bytes(), s>>>(k, kmap);
   BL_CHECK_LAUNCH("prefill_tc5_kernel");
   return BL_OK;
 }
@@ -452,6 +507,8 @@ int launch(const bl_prefill_args& a, cudaStream_t s) {
 }  // namespace
 
 int prefill_tc5_launch(const bl_prefill_args& a, cudaStream_t s) {
+  const uint64_t rows = (uint64_t)a.kv.num_layers * a.kv.num_blocks * a.kv.num_kv_heads * kBS;
+  BL_CHECK_ARG(rows + kBS <= (uint64_t)INT32_MAX, "bl_paged_prefill: pool has more than 2^31 rows");
   BL_CHECK_ARG(((uintptr_t)a.kv.k_pool & 15) == 0 && ((uintptr_t)a.kv.v_pool & 15) == 0,
                "bl_paged_prefill: pools must be 16-byte aligned");
   BL_CHECK_ARG(((uintptr_t)a.q & 3) == 0 && ((uintptr_t)a.out & 3) == 0 && a.q_stride_b % 2 == 0 &&
