@@ -183,14 +183,8 @@ extern "C" int bl_paged_prefill(const bl_prefill_args* args, void* stream) {
                "K/V sequence length must be greater than zero");
   BL_CHECK_ARG(a.kv.head_dim <= 256, "bl_paged_prefill: head_dim > 256 is not supported");
   cudaStream_t s = (cudaStream_t)stream;
-  if (prefill_tc_supported(a.kv.dtype, a.kv.head_dim, a.kv.block_size, a.num_q_heads,
-                           a.kv.num_kv_heads)) {
-    static const bool use_mma_sync = [] {
-      const char* v = getenv("BL_PREFILL_KERNEL");
-      return v && v[0] == 'm';
-    }();
-    return use_mma_sync ? prefill_tc_launch(a, s) : prefill_tc5_launch(a, s);
-  }
+  if (prefill_tc_supported(a.kv.dtype, a.kv.head_dim, a.kv.block_size, a.num_q_heads, a.kv.num_kv_heads))
+    return prefill_tc_launch(a, s);
   switch (a.kv.dtype) {
     case BL_F32: return launch_simt<float>(a, s);
     case BL_F16: return launch_simt<__half>(a, s);

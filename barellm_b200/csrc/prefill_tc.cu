@@ -1,18 +1,38 @@
-// Tensor-core paged chunked-prefill attention (bf16 / fp16, head_dim 128,
-// block_size 16, GQA group G in {1, 2, 4, 8}).
+// Paged chunked-prefill attention on 5th-generation tensor cores (tcgen05 +
+// tensor memory), bf16 / fp16, head_dim 128, block_size 16, GQA group G in
+// {1, 2, 4, 8}.
 //
-// One CTA owns a tile of 128 score rows = (128 / G) query tokens x the G
-// query heads sharing one KV head, so each K/V page is loaded once for the
-// whole GQA group.  Rows are head-major: warp w holds rows 16w..16w+15, i.e.
-// 16 consecutive query tokens of one query head.
-//   producer warp : one lane streams the row's pages through the block table,
-//                   4 pages (64 keys, 32 KiB of K+V) per stage, 3 stages, with
-//                   2-D TMA and the 128-byte swizzle.
-//   8 consumer warps : S = Q K^T and O += P V on mma.sync m16n8k16 with fp32
-//                   accumulators; Q stays in registers; online softmax in fp32;
-//                   the bottom-right causal mask is applied only on the tiles
-//                   that straddle a warp's diagonal.
-// Roofline: tensor.  Algorithmic flops per row = 4 * Hq * D * (C*P + C(C+1)/2).
+// A CTA owns 256 score rows = (256 / G) query tokens x the G query heads that
+// share one KV head, as two 128-row tiles A and B (head-major rows, so for
+// G >= 2 both tiles cover the same tokens and need the same keys).  Every K/V
+// page is fetched once for 256 rows, which halves the K/V bytes per flop of a
+// 128-row tile; keys are consumed in tiles of 128 (8 pages).  Warp roles:
+//   warps 0..1  producers: K and V pages of a key tile into 2-stage K and V
+//               rings, 16-byte cp.async per thread written in the 128-byte
+//               swizzled layout the MMA reads (paged 4 KB pages stream about
+//               four times faster this way than as 2 KB TMA boxes).  Each
+//               thread's copies arrive on the stage's mbarrier when they land;
+//               V of tile t-1 goes out before K of tile t (P V comes first).
+//               Slots past the row length or the row's last page are written
+//               as zeros (src-size 0), so stale pool bytes never reach P V.
+//   warp 2      TMEM owner (512 columns: S_A 0..127, S_B 128..255, O_A 256..383,
+//               O_B 384..511) and, on one lane, the MMA issuer.  Per key tile t
+//               it issues O_A += P_A V_{t-1}, S_A = Q_A K_t^T, O_B += P_B V_{t-1},
+//               S_B = Q_B K_t^T, so one tile's softmax runs while the tensor
+//               pipe works on the other tile.  S_X is rewritten only after the
+//               P V that read P_X (stored in S_X's columns) has completed.
+//   warps 3..6  softmax of tile A, warps 7..10 of tile B: one thread per score
+//               row (= TMEM lane).  The S row is read from TMEM once into
+//               registers (bottom-right causal mask, row max in log2 units),
+//               exponentiated and written back as packed bf16/fp16 P over the
+//               first 64 S columns, where the P V MMA reads it as its A
+//               operand; a lazy rescale touches O only when the running max
+//               grows by more than 2^8.  Epilogue: O / l from TMEM to global.
+// Every mbarrier wait is bounded; on a time-out the CTA records
+// BL_DEVERR_TIMEOUT, drains what it issued and frees its TMEM.
+// Roofline: tensor.  Algorithmic flops per request: 4 * Hq * D * (C*P + C(C+1)/2).
+#include <type_traits>
+
 #include "prefill_tc.cuh"
 
 namespace bl {
@@ -20,17 +40,29 @@ namespace {
 
 constexpr int kD = 128;
 constexpr int kBS = 16;
-constexpr int kPPT = 4;                       // pages per key tile
-constexpr int kKT = kPPT * kBS;               // 64 keys per tile
-constexpr int kNW = 8;                        // consumer warps
-constexpr int kThreads = (kNW + 1) * 32;
-constexpr int kStages = 3;
-constexpr int kPage = kBS * kD * 2;           // 4 KiB
-constexpr int kStageBytes = kPPT * 2 * kPage; // 32 KiB
-constexpr int kRows = kNW * 16;               // 128 score rows per CTA
+constexpr int kKT = 128;                 // keys per tile
+constexpr int kPPT = kKT / kBS;          // 8 pages per tile
+constexpr int kTileRows = 128;           // rows per MMA tile (M)
+constexpr int kRows = 2 * kTileRows;     // score rows per CTA
+constexpr int kKStages = 3;             // K: 3 x 32 KB (K of tile t is read after P V of t-1)
+constexpr int kVStages = 2;
+constexpr int kVProducers = 64;          // threads of warps 1..2 (V by cp.async); warp 0 issues K by TMA
+constexpr int kMmaWarp = 3;
+constexpr int kSoftmaxWarp0 = 4;
+constexpr int kThreads = 384;            // 3 producer warps, MMA warp, 2 x 4 softmax warps
+constexpr int kHalf = 128 * 128;         // 16 KB: 128 rows x 128 B (64 elements of D or K)
+constexpr int kTile = 2 * kHalf;         // 32 KB
+constexpr int kOffQ = 0;                        // + X * kTile
+constexpr int kOffK = 2 * kTile;                // + s * kTile
+constexpr int kOffV = kOffK + kKStages * kTile;  // + s * kTile
+constexpr int kSmemData = kOffV + kVStages * kTile;  // 224 KB
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColS = 0;                   // + X * 128 (P_X aliases the first 64 columns)
+constexpr uint32_t kColO = 256;                 // + X * 128
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleThreshold = 8.0f;       // log2 units
 
-struct PArgs {
+struct Args {
   const void* q;
   int64_t q_sb, q_st, q_sh;
   void* out;
@@ -41,28 +73,41 @@ struct PArgs {
   int64_t bt_stride;
   int32_t bt_width;
   const int32_t* row_ids;
-  int32_t hkv, g, bq;
+  const uint16_t* k_pool;
+  const uint16_t* v_pool;
+  int32_t q_vec16;  // q rows start on 16-byte boundaries (pointer and strides)
+  int32_t rows_total;  // rows of the K tensor map: an out-of-range row coordinate
+  int32_t hkv, g, bq;  // bq = query tokens per CTA = kRows / g
   int64_t num_blocks, layer_row0, max_q;
   float scale_log2;
   int32_t* err;
 };
 
-struct PShared {
-  uint64_t full[kStages];
-  uint64_t empty[kStages];
+struct Shared {
+  uint64_t full_k[kKStages], full_v[kVStages], empty_k[kKStages], empty_v[kVStages];
+  uint64_t s_full[2], p_full[2], pv_done[2], q_full, mma_done;
+  uint32_t tmem_base;
   int abort;
 };
 
-template <typename T>
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, Shared* sh, int32_t* err) {
+  if (*(volatile int*)&sh->abort) return false;
+  if (mbar_wait(bar, parity)) return true;
+  raise_dev(err, BL_DEVERR_TIMEOUT);
+  *(volatile int*)&sh->abort = 1;
+  return false;
+}
+
+template <bool BF16>
 __global__ void __launch_bounds__(kThreads, 1)
-    prefill_tc_kernel(const PArgs a, const __grid_constant__ CUtensorMap kmap,
-                      const __grid_constant__ CUtensorMap vmap) {
+    prefill_tc_kernel(const Args a, const __grid_constant__ CUtensorMap kmap) {
+  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  PShared* sh = reinterpret_cast<PShared*>(smem + kStages * kStageBytes);
+  Shared* sh = reinterpret_cast<Shared*>(smem + kSmemData);
 
-  // heaviest tiles (latest queries, most keys) are launched first
+  // ---- which rows: heaviest query tiles first ----
   const int64_t qtile = (int64_t)gridDim.x - 1 - blockIdx.x;
   const int h = blockIdx.y;
   const int64_t b = blockIdx.z;
@@ -77,261 +122,352 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int64_t prefix = len - nq;
   const int64_t kend = prefix + min(q0 + (int64_t)a.bq, nq);  // keys [0, kend)
   int npages = (int)((kend + kBS - 1) / kBS);
-  if (npages > a.bt_width) npages = a.bt_width;  // reported by the producer
+  const bool table_short = npages > a.bt_width;
+  if (table_short) npages = a.bt_width;
   const int ntiles = (npages + kPPT - 1) / kPPT;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&sh->full[s], 1);
-      mbar_init(&sh->empty[s], kNW);
+    for (int s = 0; s < kKStages; ++s) {
+      mbar_init(&sh->full_k[s], 1);
+      mbar_init(&sh->empty_k[s], 1);
     }
+    for (int s = 0; s < kVStages; ++s) {
+      mbar_init(&sh->full_v[s], kVProducers);
+      mbar_init(&sh->empty_v[s], 1);
+    }
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(&sh->s_full[x], 1);
+      mbar_init(&sh->p_full[x], kTileRows);
+      mbar_init(&sh->pv_done[x], 1);
+    }
+    mbar_init(&sh->q_full, kRows);
+    mbar_init(&sh->mma_done, 1);
     sh->abort = 0;
     fence_mbar_init();
   }
+  if (warp == kMmaWarp) tc_alloc(&sh->tmem_base, kTmemCols);
+  tc_fence_before();
   __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh->tmem_base;
 
-  const int64_t row = a.row_ids ? (int64_t)a.row_ids[b] : b;
-  if (warp == kNW) {
-    // ------------------------------ producer ------------------------------
-    if (lane != 0) return;
-    if ((int)((kend + kBS - 1) / kBS) > a.bt_width) raise_dev(a.err, BL_DEVERR_TABLE);
-    prefetch_tensormap(&kmap);
-    prefetch_tensormap(&vmap);
-    const int32_t* bt = a.block_tables + row * a.bt_stride;
-    int issued = 0;
+  if (warp < kMmaWarp) {
+    // ------------------------------ producers ------------------------------
+    const int64_t brow = a.row_ids ? (int64_t)a.row_ids[b] : b;
+    const int32_t* bt = a.block_tables + brow * a.bt_stride;
+    if (warp == 0) {
+      // K: one TMA per page half (64 x 16 box, 128-byte swizzle); pages past
+      // the row's last page come from an out-of-range row, which TMA fills
+      // with zeros (stale rows inside the last page are masked out of S).
+      if (lane == 0) {
+        if (table_short) raise_dev(a.err, BL_DEVERR_TABLE);
+        prefetch_tensormap(&kmap);
+        for (int t = 0; t < ntiles; ++t) {
+          const int s = t % kKStages;
+          if (!wait_or_abort(&sh->empty_k[s], ((t / kKStages) & 1) ^ 1, sh, a.err)) break;
+          unsigned char* dst = smem + kOffK + s * kTile;
+          mbar_arrive_expect_tx(&sh->full_k[s], kTile);
+#pragma unroll 1
+          for (int p = 0; p < kPPT; ++p) {
+            const int lb = t * kPPT + p;
+            int32_t y = a.rows_total;
+            if (lb < npages) {
+              const int64_t phys = bt[lb];
+              if (phys < 0 || phys >= a.num_blocks)
+                raise_dev(a.err, BL_DEVERR_BLOCK_ID);
+              else
+                y = (int32_t)(a.layer_row0 + (phys * a.hkv + h) * kBS);
+            }
+            tma_load_2d(dst + p * kBS * 128, &kmap, &sh->full_k[s], 0, y);
+            tma_load_2d(dst + kHalf + p * kBS * 128, &kmap, &sh->full_k[s], 64, y);
+          }
+        }
+        // drain: the K copies in flight land before the CTA can exit
+        const int issued = ntiles;
+        for (int s = 0; s < kKStages && s < issued; ++s) {
+          const int last = s + ((issued - 1 - s) / kKStages) * kKStages;
+          if (!mbar_wait(&sh->full_k[s], (last / kKStages) & 1)) raise_dev(a.err, BL_DEVERR_TIMEOUT);
+        }
+      }
+    } else {
+      // V: 8 pages x 16 rows x 16 chunks of 16 bytes per tile; thread vt copies
+      // chunks vt, vt + 64, ... (always chunk vt & 15 of a row); slots past the
+      // row length are zero-filled (src-size 0) so stale pool bytes never
+      // reach P V.  Lanes 0..7 look up the tile's pages, the others shuffle.
+      const int vt = threadIdx.x - 32;
+      const int cc = vt & 15;
+      const uint32_t dst_col = (uint32_t)(cc >> 3) * kHalf;
+      for (int j = 0; j < ntiles; ++j) {
+        const int s = j & 1;
+        if (!wait_or_abort(&sh->empty_v[s], ((j >> 1) & 1) ^ 1, sh, a.err)) break;
+        unsigned char* stage = smem + kOffV + s * kTile;
+        int phys_l = -1;
+        if (lane < kPPT) {
+          const int lb = j * kPPT + lane;
+          if (lb < npages) {
+            const int64_t ph = bt[lb];
+            if (ph >= 0 && ph < a.num_blocks) phys_l = (int)ph;
+          }
+        }
+        const int64_t key_t = (int64_t)j * kKT;
+#pragma unroll 4
+        for (int e = vt; e < kPPT * kBS * 16; e += kVProducers) {
+          const int p = e >> 8, r = (e >> 4) & 15;
+          const int phys = __shfl_sync(0xffffffffu, phys_l, p);
+          const uint32_t bytes = (phys >= 0 && key_t + p * kBS + r < len) ? 16u : 0u;
+          const uint16_t* src =
+              a.v_pool + ((a.layer_row0 + ((int64_t)(phys < 0 ? 0 : phys) * a.hkv + h) * kBS + r) * kD + cc * 8);
+          const uint32_t dst = smem_u32(stage + dst_col + (p * kBS + r) * 128 + (((cc & 7) ^ (r & 7)) << 4));
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+        }
+        asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&sh->full_v[s])) : "memory");
+      }
+    }
+    // every copy this thread issued lands before the CTA can exit
+    asm volatile("cp.async.wait_all;" ::: "memory");
+  } else if (warp == kMmaWarp) {
+    // ------------------------------ MMA issuer ------------------------------
+    if (lane == 0) {
+      const uint32_t idesc_s = umma_idesc_f16(kTileRows, kKT, BF16, false);
+      const uint32_t idesc_o = umma_idesc_f16(kTileRows, kD, BF16, true);
+      // O_X += P_X V_j (P_X in S_X's TMEM columns)
+      // Shared-memory descriptors are built once; an MMA's operand address is
+      // the base descriptor plus its (16-byte unit) offset, so the single
+      // issuing thread spends a few instructions per MMA (a 128 x 128 x 16 step
+      // takes 64 cycles on the tensor pipe, less than rebuilding descriptors).
+      const uint64_t dq0 = umma_desc_sw128(smem_u32(smem + kOffQ), 16, 1024);
+      const uint64_t dq1 = umma_desc_sw128(smem_u32(smem + kOffQ + kTile), 16, 1024);
+      const uint64_t dk0 = umma_desc_sw128(smem_u32(smem + kOffK), 16, 1024);
+      const uint64_t dk_stride = (uint64_t)(kTile >> 4);  // one K stage, in 16-byte units
+      const uint64_t dv0 = umma_desc_sw128(smem_u32(smem + kOffV), kHalf, 1024);
+      const uint64_t dv1 = umma_desc_sw128(smem_u32(smem + kOffV + kTile), kHalf, 1024);
+      // O_X += P_X V_j (P_X in S_X's TMEM columns)
+      auto pv = [&](int x, int j) -> bool {
+        if (!wait_or_abort(&sh->p_full[x], j & 1, sh, a.err)) return false;
+        tc_fence_after();
+        const uint64_t dv = (j & 1) ? dv1 : dv0;
+        const uint32_t d = tmem + kColO + x * 128, pa = tmem + kColS + x * 128;
+        tc_mma_ts(d, pa, dv, idesc_o, j > 0 ? 1u : 0u);
+#pragma unroll
+        for (int kk = 1; kk < kKT / 16; ++kk) tc_mma_ts(d, pa + kk * 8, dv + ((kk * 2048) >> 4), idesc_o, 1u);
+        tc_commit(&sh->pv_done[x]);
+        return true;
+      };
+      // S_X = Q_X K_t^T, once the P V that last read S_X's columns is done
+      auto qk = [&](int x, int t) -> bool {
+        if (t >= 1 && !wait_or_abort(&sh->pv_done[x], (t - 1) & 1, sh, a.err)) return false;
+        tc_fence_after();
+        const uint64_t dq = x ? dq1 : dq0, dk = dk0 + (uint64_t)(t % kKStages) * dk_stride;
+        const uint32_t d = tmem + kColS + x * 128;
+#pragma unroll
+        for (int ks = 0; ks < kD / 16; ++ks) {
+          const uint32_t off = ((ks >> 2) * kHalf + (ks & 3) * 32) >> 4;
+          tc_mma_ss(d, dq + off, dk + off, idesc_s, ks > 0 ? 1u : 0u);
+        }
+        tc_commit(&sh->s_full[x]);
+        return true;
+      };
+      // A stage's copies were written by other threads through the generic
+      // proxy; after its mbarrier completes, a proxy fence orders them before
+      // the tensor core's reads.
+      auto landed = [&](uint64_t* full, uint32_t parity) -> bool {
+        if (!wait_or_abort(full, parity, sh, a.err)) return false;
+        fence_proxy_async_smem();
+        return true;
+      };
+      // Issue order per key tile t >= 1:  PV_A(t-1), S_A(t), PV_B(t-1), S_B(t),
+      // so tile A's softmax of t runs while the tensor pipe works on tile B.
+      bool ok = wait_or_abort(&sh->q_full, 0, sh, a.err);
+      if (ok) tc_fence_after();
+      if (ok && ntiles > 0) {
+        ok = landed(&sh->full_k[0], 0) && qk(0, 0) && qk(1, 0);
+        if (ok) tc_commit(&sh->empty_k[0]);
+      }
+      for (int t = 1; t < ntiles && ok; ++t) {
+        const int j = t - 1;
+        ok = landed(&sh->full_v[j & 1], (j >> 1) & 1) && pv(0, j) &&
+             landed(&sh->full_k[t % kKStages], (t / kKStages) & 1) && qk(0, t) && pv(1, j);
+        if (!ok) break;
+        tc_commit(&sh->empty_v[j & 1]);
+        if (!(ok = qk(1, t))) break;
+        tc_commit(&sh->empty_k[t % kKStages]);
+      }
+      if (ok && ntiles > 0) {
+        const int j = ntiles - 1;
+        ok = landed(&sh->full_v[j & 1], (j >> 1) & 1) && pv(0, j) && pv(1, j);
+      }
+      // every MMA issued here has finished before the CTA tears down
+      tc_commit(&sh->mma_done);
+      if (!mbar_wait(&sh->mma_done, 0)) raise_dev(a.err, BL_DEVERR_TIMEOUT);
+    }
+  } else {
+    // ------------------------------ softmax ------------------------------
+    const int x = (warp - kSoftmaxWarp0) >> 2;  // tile: 0 = A, 1 = B
+    const int grp = warp & 3;             // TMEM lane group
+    const int tr = 32 * grp + lane;       // row within the tile == TMEM lane
+    const int r = x * kTileRows + tr;     // row within the CTA
+    const uint32_t tl = tmem + ((uint32_t)(32 * grp) << 16);
+    const uint32_t sc = kColS + x * 128, oc = kColO + x * 128;
+    const int hd = r / a.bq;
+    const int tok = r - hd * a.bq;
+    const int64_t qi = q0 + tok;
+    const bool valid = qi < nq;
+    const int hq = h * a.g + hd;
+    const int64_t lim = prefix + qi;  // inclusive key limit
+    // Q rows -> shared memory (K-major, 128-byte swizzle).  With 16-byte
+    // aligned rows the 256 softmax threads copy 16-byte chunks (a warp reads
+    // two whole 256-byte rows at a time); rows past the chunk end are zeros.
+    if (a.q_vec16) {
+      const int i = (warp - kSoftmaxWarp0) * 32 + lane;  // 0..255
+      const int qc = i & 15;
+#pragma unroll 4
+      for (int k = 0; k < 16; ++k) {
+        const int row = (i >> 4) + 16 * k;
+        const int rhd = row / a.bq, rtok = row - rhd * a.bq;
+        const int64_t rqi = q0 + rtok;
+        const bool rvalid = rqi < nq;
+        const T* src = reinterpret_cast<const T*>(a.q) + b * a.q_sb + (qo + (rvalid ? rqi : 0)) * a.q_st +
+                       (int64_t)(h * a.g + rhd) * a.q_sh + qc * 8;
+        const int rt = row & (kTileRows - 1);
+        const uint32_t dst = smem_u32(smem + kOffQ + (row >> 7) * kTile + (qc >> 3) * kHalf + rt * 128 +
+                                      (((qc & 7) ^ (rt & 7)) << 4));
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(rvalid ? 16u : 0u)
+                     : "memory");
+      }
+      asm volatile("cp.async.wait_all;" ::: "memory");
+    } else {
+      const T* qrow = reinterpret_cast<const T*>(a.q) + b * a.q_sb + (qo + (valid ? qi : 0)) * a.q_st +
+                      (int64_t)hq * a.q_sh;
+      unsigned char* qs = smem + kOffQ + x * kTile + tr * 128;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (valid) {
+          const uint32_t* src = reinterpret_cast<const uint32_t*>(qrow + c * 8);
+          v = make_uint4(src[0], src[1], src[2], src[3]);
+        }
+        *reinterpret_cast<uint4*>(qs + (c >> 3) * kHalf + (((c & 7) ^ (tr & 7)) << 4)) = v;
+      }
+    }
+    fence_proxy_async_smem();
+    mbar_arrive(&sh->q_full);
+
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
     for (int t = 0; t < ntiles; ++t) {
-      const int slot = t % kStages;
-      if (!mbar_wait(&sh->empty[slot], ((t / kStages) & 1) ^ 1)) {
-        raise_dev(a.err, BL_DEVERR_TIMEOUT);
-        sh->abort = 1;
-        break;
+      ok = __all_sync(0xffffffffu, wait_or_abort(&sh->s_full[x], t & 1, sh, a.err));
+      if (!ok) break;
+      tc_fence_after();
+      const int64_t k0 = (int64_t)t * kKT;
+      // the whole S row in registers: one TMEM read per tile
+      float v[kKT];
+#pragma unroll
+      for (int c = 0; c < kKT / 32; ++c) tc_ld32f(tl + sc + c * 32, v + c * 32);
+      tc_wait_ld();
+      reg_fence<kKT>(v);
+      // bottom-right causal mask: keys past `lim` drop out (only tiles that
+      // cross the diagonal or the chunk end take this branch)
+      const int64_t lim_rel64 = lim - k0;
+      if (__any_sync(0xffffffffu, lim_rel64 < kKT - 1)) {
+        const int lim_rel = lim_rel64 < -1 ? -1 : (int)lim_rel64;
+#pragma unroll
+        for (int j = 0; j < kKT; ++j) v[j] = j > lim_rel ? -INFINITY : v[j];
       }
-      const int np = min(kPPT, npages - t * kPPT);
-      unsigned char* st = smem + slot * kStageBytes;
-      mbar_arrive_expect_tx(&sh->full[slot], np * 2 * kPage);
-      for (int p = 0; p < np; ++p) {
-        int64_t phys = bt[t * kPPT + p];
-        if (phys < 0 || phys >= a.num_blocks) {
-          raise_dev(a.err, BL_DEVERR_BLOCK_ID);
-          phys = 0;
+      // row max of the raw scores (the scale is positive), eight partial chains
+      float mp[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mp[i] = v[i];
+#pragma unroll
+      for (int j = 8; j < kKT; ++j) mp[j & 7] = fmaxf(mp[j & 7], v[j]);
+      const float mt = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
+                             fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7]))) * a.scale_log2;
+      const float m_new = fmaxf(m_used, mt);
+      const bool need = (t > 0) && (m_new > m_used + kRescaleThreshold);
+      const float alpha = need ? fast_exp2(m_used - m_new) : 1.f;
+      if (need || t == 0) m_used = m_new;
+      const float ms = (m_used == -INFINITY) ? 0.f : m_used;
+      // P = exp2(s * scale - m), packed two per column over S's first 64
+      // columns (S is already in registers)
+      float rp[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < kKT / 32; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float p0 = fast_exp2(fmaf(v[c * 32 + 2 * j], a.scale_log2, -ms));
+          const float p1 = fast_exp2(fmaf(v[c * 32 + 2 * j + 1], a.scale_log2, -ms));
+          rp[j & 3] += p0 + p1;
+          pk[j] = pack2<T>(p0, p1);
         }
-        const int32_t y = (int32_t)(a.layer_row0 + (phys * a.hkv + h) * kBS);
-        unsigned char* kd = st + p * kPage;
-        unsigned char* vd = st + kPPT * kPage + p * kPage;
-        tma_load_2d(kd, &kmap, &sh->full[slot], 0, y);
-        tma_load_2d(kd + kPage / 2, &kmap, &sh->full[slot], 64, y);
-        tma_load_2d(vd, &vmap, &sh->full[slot], 0, y);
-        tma_load_2d(vd + kPage / 2, &vmap, &sh->full[slot], 64, y);
+        tc_st16(tl + sc + c * 16, pk);
       }
-      ++issued;
-    }
-    for (int s = 0; s < kStages && s < issued; ++s) {
-      const int last = s + ((issued - 1 - s) / kStages) * kStages;
-      if (!mbar_wait(&sh->full[s], (last / kStages) & 1)) raise_dev(a.err, BL_DEVERR_TIMEOUT);
-    }
-    return;
-  }
-
-  // ------------------------------ consumers ------------------------------
-  const int g_row = lane >> 2;
-  const int t4 = lane & 3;
-  const int m0 = warp * 16;
-  const int hd = m0 / a.bq;
-  const int tok0 = m0 - hd * a.bq;
-  const int hq = h * a.g + hd;
-  const int64_t i0 = q0 + tok0 + g_row;  // query index of rows g_row / g_row + 8
-  const int64_t i1 = i0 + 8;
-  const bool v0 = i0 < nq, v1 = i1 < nq;
-  const int64_t lim0 = prefix + i0, lim1 = prefix + i1;  // inclusive key limits
-  const int64_t warp_min_lim = prefix + q0 + tok0;
-  const int64_t warp_max_lim = prefix + min(q0 + tok0 + 15, nq - 1);
-
-  uint32_t qf[8][4];
-  {
-    const T* qb = reinterpret_cast<const T*>(a.q) + b * a.q_sb + (int64_t)hq * a.q_sh;
-    const T* q0p = qb + (qo + (v0 ? i0 : 0)) * a.q_st;
-    const T* q1p = qb + (qo + (v1 ? i1 : 0)) * a.q_st;
+      const float rs = (rp[0] + rp[1]) + (rp[2] + rp[3]);
+      // lazy rescale of O (the P V that last wrote O_X completed before S_X was
+      // issued); rare once the running max has settled
+      if (__any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float o[32];
+          tc_ld32f(tl + oc + c * 32, o);
+          tc_wait_ld();
+          reg_fence<32>(o);
 #pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      const int c = ks * 16 + 2 * t4;
-      qf[ks][0] = v0 ? *reinterpret_cast<const uint32_t*>(q0p + c) : 0u;
-      qf[ks][1] = v1 ? *reinterpret_cast<const uint32_t*>(q1p + c) : 0u;
-      qf[ks][2] = v0 ? *reinterpret_cast<const uint32_t*>(q0p + c + 8) : 0u;
-      qf[ks][3] = v1 ? *reinterpret_cast<const uint32_t*>(q1p + c + 8) : 0u;
-    }
-  }
-
-  float o[16][4];
-#pragma unroll
-  for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-  float mr0 = -INFINITY, mr1 = -INFINITY, lr0 = 0.f, lr1 = 0.f;
-
-  // per-lane ldmatrix geometry
-  const int key_k = (lane & 7) + ((lane >> 4) << 3);  // K (non-trans) rows
-  const int hi_k = (lane >> 3) & 1;
-  const int key_v = (lane & 7) + (((lane >> 3) & 1) << 3);  // V (trans) rows
-  const int hi_v = lane >> 4;
-
-  for (int t = 0; t < ntiles; ++t) {
-    const int slot = t % kStages;
-    if (*(volatile int*)&sh->abort) break;
-    if (!mbar_wait(&sh->full[slot], (t / kStages) & 1)) {
-      raise_dev(a.err, BL_DEVERR_TIMEOUT);
-      *(volatile int*)&sh->abort = 1;
-      break;
-    }
-    const int np = min(kPPT, npages - t * kPPT);
-    const int64_t kt0 = (int64_t)t * kKT;
-    if (kt0 <= warp_max_lim) {
-      const uint32_t kst = smem_u32(smem + slot * kStageBytes);
-      const uint32_t vst = kst + kPPT * kPage;
-      float s[8][4];
-#pragma unroll
-      for (int n = 0; n < 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const int cc = 2 * (ks & 3) + hi_k;
-        const uint32_t off = (ks >> 2) * (kPage / 2) + key_k * 128 + ((cc ^ (key_k & 7)) << 4);
-#pragma unroll
-        for (int p = 0; p < kPPT; ++p) {
-          if (p < np) {
-            uint32_t r0, r1, r2, r3;
-            ldmatrix_x4(kst + p * kPage + off, r0, r1, r2, r3);
-            mma_16816<T>(s[2 * p][0], s[2 * p][1], s[2 * p][2], s[2 * p][3], qf[ks][0], qf[ks][1],
-                         qf[ks][2], qf[ks][3], r0, r1);
-            mma_16816<T>(s[2 * p + 1][0], s[2 * p + 1][1], s[2 * p + 1][2], s[2 * p + 1][3],
-                         qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3], r2, r3);
-          }
+          for (int j = 0; j < 32; ++j) o[j] *= alpha;
+          tc_st32f(tl + oc + c * 32, o);
         }
       }
-      // scale + causal mask (only where this tile crosses the warp's diagonal)
-      const bool need_mask = (kt0 + kKT - 1 > warp_min_lim) || (np < kPPT);
+      tc_wait_st();
+      l = l * alpha + rs;
+      tc_fence_before();
+      mbar_arrive(&sh->p_full[x]);
+    }
+    // ---- epilogue ----
+    if (ok && ntiles > 0) {
+      ok = __all_sync(0xffffffffu, wait_or_abort(&sh->pv_done[x], (ntiles - 1) & 1, sh, a.err));
+      if (ok) {
+        tc_fence_after();
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        T* orow = reinterpret_cast<T*>(a.out) + b * a.o_sb + (qo + (valid ? qi : 0)) * a.o_st + (int64_t)hq * a.o_sh;
 #pragma unroll
-      for (int n = 0; n < 8; ++n) {
+        for (int c = 0; c < 4; ++c) {
+          float o[32];
+          tc_ld32f(tl + oc + c * 32, o);
+          tc_wait_ld();
+          reg_fence<32>(o);
+          if (valid) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) s[n][c] *= a.scale_log2;
-        if (need_mask) {
-          const int64_t key = kt0 + 8 * n + 2 * t4;
-          const bool loaded = (n >> 1) < np;
-          if (!loaded || key > lim0) s[n][0] = -INFINITY;
-          if (!loaded || key + 1 > lim0) s[n][1] = -INFINITY;
-          if (!loaded || key > lim1) s[n][2] = -INFINITY;
-          if (!loaded || key + 1 > lim1) s[n][3] = -INFINITY;
-        }
-      }
-      float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-      for (int n = 0; n < 8; ++n) {
-        mx0 = fmaxf(mx0, fmaxf(s[n][0], s[n][1]));
-        mx1 = fmaxf(mx1, fmaxf(s[n][2], s[n][3]));
-      }
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-      const float mn0 = fmaxf(mr0, mx0), mn1 = fmaxf(mr1, mx1);
-      const float ms0 = (mn0 == -INFINITY) ? 0.f : mn0;  // fully masked so far
-      const float ms1 = (mn1 == -INFINITY) ? 0.f : mn1;
-      const float al0 = fast_exp2(mr0 - ms0), al1 = fast_exp2(mr1 - ms1);
-      mr0 = mn0;
-      mr1 = mn1;
-      float rs0 = 0.f, rs1 = 0.f;
-#pragma unroll
-      for (int n = 0; n < 8; ++n) {
-        s[n][0] = fast_exp2(s[n][0] - ms0);
-        s[n][1] = fast_exp2(s[n][1] - ms0);
-        s[n][2] = fast_exp2(s[n][2] - ms1);
-        s[n][3] = fast_exp2(s[n][3] - ms1);
-        rs0 += s[n][0] + s[n][1];
-        rs1 += s[n][2] + s[n][3];
-      }
-      lr0 = lr0 * al0 + rs0;
-      lr1 = lr1 * al1 + rs1;
-#pragma unroll
-      for (int n = 0; n < 16; ++n) {
-        o[n][0] *= al0;
-        o[n][1] *= al0;
-        o[n][2] *= al1;
-        o[n][3] *= al1;
-      }
-      // O += P V
-#pragma unroll
-      for (int kk = 0; kk < kPPT; ++kk) {
-        if (kk < np) {
-          const uint32_t pa0 = pack2<T>(s[2 * kk][0], s[2 * kk][1]);
-          const uint32_t pa1 = pack2<T>(s[2 * kk][2], s[2 * kk][3]);
-          const uint32_t pa2 = pack2<T>(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-          const uint32_t pa3 = pack2<T>(s[2 * kk + 1][2], s[2 * kk + 1][3]);
-          // keys past the row length hold stale pool bytes: zero them
-          const int64_t pk0 = kt0 + kk * kBS;
-          uint32_t mlo = 0xffffffffu, mhi = 0xffffffffu;
-          if (pk0 + kBS > len) {
-            const int64_t nv = len - pk0;
-            mlo = (2 * t4 < nv ? 0x0000ffffu : 0u) | (2 * t4 + 1 < nv ? 0xffff0000u : 0u);
-            mhi = (8 + 2 * t4 < nv ? 0x0000ffffu : 0u) | (9 + 2 * t4 < nv ? 0xffff0000u : 0u);
-          }
-          const uint32_t vpg = vst + kk * kPage;
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const int cc = 2 * (j & 3) + hi_v;
-            const uint32_t addr = vpg + (j >> 2) * (kPage / 2) + key_v * 128 + ((cc ^ (key_v & 7)) << 4);
-            uint32_t r0, r1, r2, r3;
-            ldmatrix_x4_trans(addr, r0, r1, r2, r3);
-            mma_16816<T>(o[2 * j][0], o[2 * j][1], o[2 * j][2], o[2 * j][3], pa0, pa1, pa2, pa3,
-                         r0 & mlo, r1 & mhi);
-            mma_16816<T>(o[2 * j + 1][0], o[2 * j + 1][1], o[2 * j + 1][2], o[2 * j + 1][3], pa0, pa1,
-                         pa2, pa3, r2 & mlo, r3 & mhi);
+            for (int j = 0; j < 16; ++j)
+              reinterpret_cast<uint32_t*>(orow + c * 32)[j] = pack2<T>(o[2 * j] * inv, o[2 * j + 1] * inv);
           }
         }
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&sh->empty[slot]);
   }
 
-  // ---- epilogue: normalise and store ----
-  lr0 += __shfl_xor_sync(0xffffffffu, lr0, 1);
-  lr0 += __shfl_xor_sync(0xffffffffu, lr0, 2);
-  lr1 += __shfl_xor_sync(0xffffffffu, lr1, 1);
-  lr1 += __shfl_xor_sync(0xffffffffu, lr1, 2);
-  const float inv0 = lr0 > 0.f ? 1.f / lr0 : 0.f;
-  const float inv1 = lr1 > 0.f ? 1.f / lr1 : 0.f;
-  T* ob = reinterpret_cast<T*>(a.out) + b * a.o_sb + (int64_t)hq * a.o_sh;
-  if (v0) {
-    T* op = ob + (qo + i0) * a.o_st;
-#pragma unroll
-    for (int n = 0; n < 16; ++n)
-      *reinterpret_cast<uint32_t*>(op + 8 * n + 2 * t4) = pack2<T>(o[n][0] * inv0, o[n][1] * inv0);
-  }
-  if (v1) {
-    T* op = ob + (qo + i1) * a.o_st;
-#pragma unroll
-    for (int n = 0; n < 16; ++n)
-      *reinterpret_cast<uint32_t*>(op + 8 * n + 2 * t4) = pack2<T>(o[n][2] * inv1, o[n][3] * inv1);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tc_dealloc(tmem, kTmemCols);
   }
 }
 
-size_t smem_bytes() { return 1024 + kStages * kStageBytes + sizeof(PShared); }
+size_t smem_bytes() { return 1024 + kSmemData + sizeof(Shared); }
 
-template <typename T>
+template <bool BF16>
 int launch(const bl_prefill_args& a, cudaStream_t s) {
   static bool attr_done = false;
   if (!attr_done) {
-    if (cudaFuncSetAttribute(prefill_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(prefill_tc_kernel<BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)smem_bytes()) != cudaSuccess) {
       set_error("prefill: cudaFuncSetAttribute failed");
       return BL_ERR_LAUNCH;
     }
     attr_done = true;
   }
-  const uint64_t rows = (uint64_t)a.kv.num_layers * a.kv.num_blocks * a.kv.num_kv_heads * kBS;
-  CUtensorMap kmap, vmap;
-  if (!get_pool_tmap(a.kv.k_pool, rows, a.kv.dtype, &kmap) ||
-      !get_pool_tmap(a.kv.v_pool, rows, a.kv.dtype, &vmap))
-    return BL_ERR_LAUNCH;
-  PArgs k;
+  Args k;
   k.q = a.q;
   k.q_sb = a.q_stride_b;
   k.q_st = a.q_stride_t;
@@ -352,11 +488,18 @@ int launch(const bl_prefill_args& a, cudaStream_t s) {
   k.num_blocks = a.kv.num_blocks;
   k.layer_row0 = (int64_t)a.kv.layer * a.kv.num_blocks * a.kv.num_kv_heads * kBS;
   k.max_q = a.max_q_len;
+  const uint64_t rows = (uint64_t)a.kv.num_layers * a.kv.num_blocks * a.kv.num_kv_heads * kBS;
+  CUtensorMap kmap;
+  if (!get_pool_tmap(a.kv.k_pool, rows, a.kv.dtype, &kmap)) return BL_ERR_LAUNCH;
+  k.rows_total = (int32_t)rows;
+  k.q_vec16 = ((uintptr_t)a.q % 16 == 0) && a.q_stride_b % 8 == 0 && a.q_stride_t % 8 == 0 && a.q_stride_h % 8 == 0;
+  k.k_pool = static_cast<const uint16_t*>(a.kv.k_pool);
+  k.v_pool = static_cast<const uint16_t*>(a.kv.v_pool);
   k.scale_log2 = a.scale * kLog2e;
   k.err = a.err;
   const int64_t tiles = (a.max_q_len + k.bq - 1) / k.bq;
   dim3 grid((unsigned)tiles, (unsigned)a.kv.num_kv_heads, (unsigned)a.batch);
-  prefill_tc_kernel<T><<<grid, kThreads, smem_bytes(), s>>>(k, kmap, vmap);
+  prefill_tc_kernel<BF16><<<grid, kThreads, smem_bytes(), s>>>(k, kmap);
   BL_CHECK_LAUNCH("prefill_tc_kernel");
   return BL_OK;
 }
@@ -373,15 +516,15 @@ bool prefill_tc_supported(int32_t dtype, int64_t head_dim, int64_t block_size, i
 
 int prefill_tc_launch(const bl_prefill_args& a, cudaStream_t s) {
   const uint64_t rows = (uint64_t)a.kv.num_layers * a.kv.num_blocks * a.kv.num_kv_heads * kBS;
-  BL_CHECK_ARG(rows <= (uint64_t)INT32_MAX, "bl_paged_prefill: pool has more than 2^31 rows");
+  BL_CHECK_ARG(rows + kBS <= (uint64_t)INT32_MAX, "bl_paged_prefill: pool has more than 2^31 rows");
   BL_CHECK_ARG(((uintptr_t)a.kv.k_pool & 15) == 0 && ((uintptr_t)a.kv.v_pool & 15) == 0,
                "bl_paged_prefill: pools must be 16-byte aligned");
   BL_CHECK_ARG(((uintptr_t)a.q & 3) == 0 && ((uintptr_t)a.out & 3) == 0 && a.q_stride_b % 2 == 0 &&
                    a.q_stride_t % 2 == 0 && a.q_stride_h % 2 == 0 && a.out_stride_b % 2 == 0 &&
                    a.out_stride_t % 2 == 0 && a.out_stride_h % 2 == 0,
                "bl_paged_prefill: q/out must be 4-byte aligned with even strides");
-  if (a.kv.dtype == BL_BF16) return launch<__nv_bfloat16>(a, s);
-  return launch<__half>(a, s);
+  if (a.kv.dtype == BL_BF16) return launch<true>(a, s);
+  return launch<false>(a, s);
 }
 
 }  // namespace bl

@@ -959,7 +959,11 @@ def main() -> None:
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode_qwen06b_b64")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--pool-blocks", type=int, default=0,
+                    help="override the KV pool size in blocks (smaller profiling captures)")
     args = ap.parse_args()
+    if args.pool_blocks > 0 and "pool_blocks" in WORKLOADS[args.workload]:
+        WORKLOADS[args.workload]["pool_blocks"] = args.pool_blocks
     if args.warmup < 3:
         args.warmup = 3
     kind = WORKLOADS[args.workload].get("kind")
