@@ -46,6 +46,7 @@ struct AppendKernelArgs {
 // walk one page row after another.
 template <int VEC>
 __global__ void __launch_bounds__(256) paged_append_kernel(const AppendKernelArgs a) {
+  pdl_trigger();  // a dependent launch (the decode plan) may start; it waits for this grid
   using V = typename VecT<VEC>::type;
   const int64_t b = blockIdx.y;
   const uint32_t idx = blockIdx.x * blockDim.x + threadIdx.x;

@@ -11,6 +11,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <utility>
 
 #include "../../include/barellm_b200.h"
 
@@ -37,6 +38,24 @@ void set_error(const char* fmt, ...);
       return BL_ERR_LAUNCH;                                                   \
     }                                                                         \
   } while (0)
+
+// Launches `kernel` so that it may overlap the tail of the previous kernel on
+// the stream (the kernel calls pdl_wait() before reading that kernel's output).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 inline int elem_size(int32_t dtype) {
   switch (dtype) {
@@ -99,6 +118,14 @@ __device__ __forceinline__ void raise_dev(int32_t* err, int32_t bit) {
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
+
+// Programmatic dependent launch: a kernel launched with
+// launch_pdl() may start while the previous kernel on the stream still runs;
+// pdl_wait() blocks until that kernel has completed and its writes are
+// visible (a no-op without a programmatic predecessor).  pdl_trigger() lets
+// the next such kernel start early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 __device__ __forceinline__ uint64_t global_timer_ns() {
   uint64_t t;

@@ -24,6 +24,12 @@
 //                           through shared memory; single-chunk rows write the
 //                           output, others write (o, lse) partials.
 //   decode_reduce_kernel    merges the partials of multi-chunk rows.
+// The plan, attention and reduce kernels are launched with programmatic
+// dependent launch: each may start while its predecessor finishes and waits
+// (griddepcontrol.wait) before reading that predecessor's output.  (Merging
+// split rows inside the attention kernel, by the CTA that finishes a row's
+// last chunk, measured slower: the merge and its fences stall that CTA's page
+// pipeline.)
 //   decode_simt_kernel      any dtype / head_dim <= 256 / block_size / group:
 //                           one CTA per (row, q-head), no split.
 // Roofline: HBM.  Algorithmic bytes per launch = sum_b len_b * Hkv * D * 2 * E
@@ -114,6 +120,9 @@ __device__ __forceinline__ int row_blocks(int len, int bs, int bt_width, int32_t
 }
 
 __global__ void __launch_bounds__(kPlanThreads) decode_plan_kernel(const PlanArgs a) {
+  // the attention kernel may launch now; it waits for this grid (and, through
+  // the pdl_wait below, for the append before it) before reading the plan
+  pdl_trigger();
   __shared__ int warp_tot[32];
   __shared__ int hist[kChunkTokens + 1];    // partial-chunk sizes (blocks), 1..chunk_blocks-1
   __shared__ int bucket[kChunkTokens + 1];
@@ -170,6 +179,8 @@ __global__ void __launch_bounds__(kPlanThreads) decode_plan_kernel(const PlanArg
       if (p < a.max_units) a.exec[p] = make_int2(b, nfull);
     }
   }
+  // complete only after the previous kernel (the step's K/V append) has
+  pdl_wait();
 }
 
 // ---------------------------------------------------------------------------
@@ -241,6 +252,7 @@ __global__ void __launch_bounds__(kThreadsTC) decode_tc_kernel(const TCArgs a,
   }
   __syncthreads();
 
+  pdl_wait();  // the plan (and the append before it) are complete and visible
   const int total_items = a.hdr[0] * a.hkv;
   const int cb = a.chunk_blocks;
 
@@ -484,6 +496,7 @@ struct ReduceArgs {
 // grid (batch, hq); block = d threads
 template <typename T>
 __global__ void __launch_bounds__(256) decode_reduce_kernel(const ReduceArgs a) {
+  pdl_wait();  // the attention kernel's partials are complete and visible
   const int b = blockIdx.x;
   const int hq = blockIdx.y;
   const int len = a.seq_lens[b];
@@ -681,8 +694,11 @@ int launch_tc_attention(const bl_decode_args& a, const WsLayout& w, cudaStream_t
 
   const int64_t item_bound = w.max_units * a.kv.num_kv_heads;
   const int64_t grid = std::min<int64_t>((int64_t)num_sms() * occ, item_bound);
-  decode_tc_kernel<T><<<(unsigned)grid, kThreadsTC, smem, s>>>(k, kmap, vmap);
-  BL_CHECK_LAUNCH("decode_tc_kernel");
+  if (launch_pdl(decode_tc_kernel<T>, dim3((unsigned)grid), dim3(kThreadsTC), smem, s, k, kmap, vmap) !=
+      cudaSuccess) {
+    set_error("decode_tc_kernel: launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+    return BL_ERR_LAUNCH;
+  }
   return BL_OK;
 }
 
@@ -703,8 +719,11 @@ int launch_tc_reduce(const bl_decode_args& a, const WsLayout& w, cudaStream_t s)
   r.ws_lse = (const float*)(ws + w.lse);
   r.ws_o = (const float*)(ws + w.o);
   r.max_units = (int32_t)w.max_units;
-  decode_reduce_kernel<T><<<dim3((unsigned)a.batch, (unsigned)a.num_q_heads), kD, 0, s>>>(r);
-  BL_CHECK_LAUNCH("decode_reduce_kernel");
+  if (launch_pdl(decode_reduce_kernel<T>, dim3((unsigned)a.batch, (unsigned)a.num_q_heads), dim3(kD), 0, s, r) !=
+      cudaSuccess) {
+    set_error("decode_reduce_kernel: launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+    return BL_ERR_LAUNCH;
+  }
   return BL_OK;
 }
 
@@ -793,8 +812,10 @@ extern "C" int bl_paged_decode_plan(const bl_decode_args* args, void* stream) {
   p.row_base = (int32_t*)(ws + w.row_base);
   p.exec = (int2*)(ws + w.exec);
   p.err = a.err;
-  decode_plan_kernel<<<1, kPlanThreads, 0, (cudaStream_t)stream>>>(p);
-  BL_CHECK_LAUNCH("decode_plan_kernel");
+  if (launch_pdl(decode_plan_kernel, dim3(1), dim3(kPlanThreads), 0, (cudaStream_t)stream, p) != cudaSuccess) {
+    set_error("decode_plan_kernel: launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+    return BL_ERR_LAUNCH;
+  }
   return BL_OK;
 }
 

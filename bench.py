@@ -6,7 +6,8 @@
 
 One step is one pass of the hot path over one batch: the one-token K/V append
 of every request, the split-K plan, the decode attention kernel and the
-split-K reduce (4 kernels, replayed as one CUDA graph).  Default workload:
+split-K reduce (4 kernels, replayed as one CUDA graph, each starting early
+through programmatic dependent launch).  Default workload:
 batched paged decode at Qwen3-0.6B attention shapes (16 q / 8 kv heads,
 head_dim 128, block_size 16), bf16, 64 requests per GPU with history lengths
 ~U{128..4096}, blocks shuffled across a 65536-block pool, Q/K/V ~ N(0,1)/sqrt(128).
@@ -167,7 +168,8 @@ class DecodeWorkload:
         return kv + qo
 
     def step(self) -> None:
-        """append -> plan -> attention -> reduce (4 kernel launches)."""
+        """append -> plan -> attention -> reduce (4 kernel launches; plan,
+        attention and reduce start early through programmatic dependent launch)."""
         from barellm_b200 import ops
 
         ops.paged_append(self.k_cache, self.v_cache, 0, self.bt, self.starts, self.k_new, self.v_new, err=self.err)
