@@ -32,6 +32,7 @@ BL_DEVERR_WORKSPACE = 8
 
 EXPORTED = (
     "bl_paged_append",
+    "bl_qk_norm_rope_append",
     "bl_paged_gather",
     "bl_paged_decode_workspace_bytes",
     "bl_paged_decode_plan",
@@ -142,8 +143,45 @@ class PrefillArgs(Structure):
     ]
 
 
+class QkPrepArgs(Structure):
+    _fields_ = [
+        ("kv", PagedLayer),
+        ("q_in", c_void_p),
+        ("q_in_stride_b", c_int64),
+        ("q_in_stride_h", c_int64),
+        ("q_in_stride_t", c_int64),
+        ("k_in", c_void_p),
+        ("k_in_stride_b", c_int64),
+        ("k_in_stride_h", c_int64),
+        ("k_in_stride_t", c_int64),
+        ("v_in", c_void_p),
+        ("v_in_stride_b", c_int64),
+        ("v_in_stride_h", c_int64),
+        ("v_in_stride_t", c_int64),
+        ("q_out", c_void_p),
+        ("q_out_stride_b", c_int64),
+        ("q_out_stride_h", c_int64),
+        ("q_out_stride_t", c_int64),
+        ("q_norm_weight", c_void_p),
+        ("k_norm_weight", c_void_p),
+        ("cos", c_void_p),
+        ("sin", c_void_p),
+        ("rope_stride_b", c_int64),
+        ("rope_stride_t", c_int64),
+        ("eps", c_float),
+        ("pad0", c_int32),
+        ("num_q_heads", c_int64),
+        ("start_pos", c_void_p),
+        ("new_offsets", c_void_p),
+        ("batch", c_int64),
+        ("max_new_tokens", c_int64),
+        ("err", c_void_p),
+    ]
+
+
 STRUCTS = {
     "bl_paged_layer": PagedLayer,
+    "bl_qk_prep_args": QkPrepArgs,
     "bl_append_args": AppendArgs,
     "bl_gather_args": GatherArgs,
     "bl_decode_args": DecodeArgs,
@@ -166,6 +204,8 @@ def load() -> ctypes.CDLL:
     lib = ctypes.CDLL(str(LIB_PATH))
     lib.bl_paged_append.argtypes = [POINTER(AppendArgs), c_void_p]
     lib.bl_paged_append.restype = c_int
+    lib.bl_qk_norm_rope_append.argtypes = [POINTER(QkPrepArgs), c_void_p]
+    lib.bl_qk_norm_rope_append.restype = c_int
     lib.bl_paged_gather.argtypes = [POINTER(GatherArgs), c_void_p]
     lib.bl_paged_gather.restype = c_int
     lib.bl_paged_decode_workspace_bytes.argtypes = [c_int64] * 5

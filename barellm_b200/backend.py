@@ -52,8 +52,28 @@ class CudaPagedAttentionBackend:
             return self._uncached(q, new_k, new_v)
         raise TypeError(f"the cuda attention backend reads paged caches, not {type(layer_cache).__name__}")
 
+    def attend_prepped(self, q: torch.Tensor, new_k: torch.Tensor, new_v: torch.Tensor, q_norm_weight: torch.Tensor,
+                       k_norm_weight: torch.Tensor, eps: float, cos: torch.Tensor, sin: torch.Tensor, layer_cache,
+                       group_size: int) -> torch.Tensor:
+        """``attend`` for q / new_k straight out of the projections: the
+        QK-RMSNorm and RoPE of the reference's attention
+        (src/barellm/models/attention.py:161-169) run fused with the append
+        (one kernel), then the same paged attention as ``attend``."""
+        check(q.ndim == 4 and new_k.ndim == 4, "q/K/V must have shape [B, H, T, D]")
+        check(q.shape[1] == new_k.shape[1] * group_size, "num_heads must divide evenly by num_kv_heads")
+        if isinstance(layer_cache, BatchLayerKV):
+            meta, qp = layer_cache.append_only_prepped(q, new_k, new_v, q_norm_weight, k_norm_weight, cos, sin, eps)
+            return self._batched_attend(qp, layer_cache, meta)
+        if isinstance(layer_cache, PagedLayerKV):
+            check(q.shape[0] == 1, "PagedKVCache currently supports batch size 1")
+            qp = layer_cache.append_only_prepped(q, new_k, new_v, q_norm_weight, k_norm_weight, cos, sin, eps)
+            return self._single_attend(qp, layer_cache)
+        raise TypeError("fused QK preparation needs a paged cache; use attend() with prepared q/k")
+
     def _batched(self, q, new_k, new_v, layer: BatchLayerKV) -> torch.Tensor:
-        meta = layer.append_only(new_k, new_v)
+        return self._batched_attend(q, layer, layer.append_only(new_k, new_v))
+
+    def _batched_attend(self, q, layer: BatchLayerKV, meta) -> torch.Tensor:
         s = layer.storage()
         idx = layer.layer_idx
         if q.shape[2] == 1:
@@ -73,6 +93,9 @@ class CudaPagedAttentionBackend:
     def _single(self, q, new_k, new_v, layer: PagedLayerKV) -> torch.Tensor:
         check(q.shape[0] == 1, "PagedKVCache currently supports batch size 1")
         layer.append_only(new_k, new_v)
+        return self._single_attend(q, layer)
+
+    def _single_attend(self, q, layer: PagedLayerKV) -> torch.Tensor:
         s = layer.storage
         n = layer.seq_len
         rows = _i32([layer._request.row], s.device)

@@ -170,10 +170,7 @@ class BatchLayerKV:
         self.append_only(key, value)
         return self.read()
 
-    def append_only(self, key: torch.Tensor, value: torch.Tensor) -> StepMeta:
-        """One scatter kernel for every row (reference: a Python loop of
-        per-row appends, batched_kv_cache.py:40-63).  Returns the step metadata
-        whose ``seq_lens`` are the post-append lengths."""
+    def _begin_append(self, key: torch.Tensor, value: torch.Tensor):
         b = len(self.owner.caches)
         check(key.shape[0] == b, "batch size must match number of caches")
         check(value.shape[0] == b, "batch size must match number of caches")
@@ -185,11 +182,30 @@ class BatchLayerKV:
         ends = starts + t
         need = (ends + s.block_size - 1) // s.block_size
         check(bool((need <= s.arena.used[rows]).all()), "request does not have enough allocated KV blocks")
-        meta = self.owner.step_meta(starts, t)
+        return s, rows, ends, self.owner.step_meta(starts, t)
+
+    def append_only(self, key: torch.Tensor, value: torch.Tensor) -> StepMeta:
+        """One scatter kernel for every row (reference: a Python loop of
+        per-row appends, batched_kv_cache.py:40-63).  Returns the step metadata
+        whose ``seq_lens`` are the post-append lengths."""
+        s, rows, ends, meta = self._begin_append(key, value)
         ops.paged_append(s.key_cache, s.value_cache, self.layer_idx, s.arena.table, meta.starts, key, value,
                          row_ids=meta.rows, err=s.err)
         s.arena.lens[rows, self.layer_idx] = ends
         return meta
+
+    def append_only_prepped(self, q: torch.Tensor, key: torch.Tensor, value: torch.Tensor, q_norm_weight,
+                            k_norm_weight, cos, sin, eps: float) -> tuple[StepMeta, torch.Tensor]:
+        """append_only of the QK-normalised, rotated key, with the same norm and
+        rotation applied to ``q``, in one kernel (see
+        ``ops.qk_norm_rope_append``).  Returns the step metadata and the
+        prepared q."""
+        s, rows, ends, meta = self._begin_append(key, value)
+        q_out = ops.qk_norm_rope_append(q, key, value, q_norm_weight, k_norm_weight, cos, sin, eps, s.key_cache,
+                                        s.value_cache, self.layer_idx, s.arena.table, meta.starts,
+                                        row_ids=meta.rows, err=s.err)
+        s.arena.lens[rows, self.layer_idx] = ends
+        return meta, q_out
 
     def current_meta(self) -> StepMeta:
         """Metadata whose post-append lengths equal the current lengths."""

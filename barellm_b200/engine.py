@@ -82,6 +82,7 @@ class Attention(nn.Module):
         self.q_norm = RMSNorm(s.head_dim, s.rms_norm_eps)
         self.k_norm = RMSNorm(s.head_dim, s.rms_norm_eps)
         self.backend = backend
+        self.fused_prep = True  # QK-norm + RoPE + append in one kernel when the cache is paged
 
     def forward(self, x, cos, sin, layer_cache) -> torch.Tensor:
         b, t, _ = x.shape
@@ -89,9 +90,16 @@ class Attention(nn.Module):
         q = self.q_proj(x).view(b, t, s.num_heads, s.head_dim).transpose(1, 2)
         k = self.k_proj(x).view(b, t, s.num_kv_heads, s.head_dim).transpose(1, 2)
         v = self.v_proj(x).view(b, t, s.num_kv_heads, s.head_dim).transpose(1, 2)
-        q = apply_rope(self.q_norm(q), cos, sin)
-        k = apply_rope(self.k_norm(k), cos, sin)
-        ctx = self.backend.attend(q, k, v, layer_cache, s.num_heads // s.num_kv_heads)
+        group = s.num_heads // s.num_kv_heads
+        prepped = getattr(self.backend, "attend_prepped", None)
+        if self.fused_prep and prepped is not None and layer_cache is not None:
+            # QK-norm + RoPE fused with the paged append (one kernel)
+            ctx = prepped(q, k, v, self.q_norm.weight, self.k_norm.weight, self.q_norm.eps, cos, sin, layer_cache,
+                          group)
+        else:
+            q = apply_rope(self.q_norm(q), cos, sin)
+            k = apply_rope(self.k_norm(k), cos, sin)
+            ctx = self.backend.attend(q, k, v, layer_cache, group)
         return self.o_proj(ctx.transpose(1, 2).reshape(b, t, -1))
 
 

@@ -152,6 +152,93 @@ def paged_append(
     _raise_rc(nat.load().bl_paged_append(a, _stream(key.device)))
 
 
+def qk_norm_rope_append(
+    q: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    q_norm_weight: torch.Tensor,
+    k_norm_weight: torch.Tensor,
+    cos: torch.Tensor,
+    sin: torch.Tensor,
+    eps: float,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    layer: int,
+    block_tables: torch.Tensor,
+    start_pos: torch.Tensor,
+    *,
+    row_ids: torch.Tensor | None = None,
+    new_offsets: torch.Tensor | None = None,
+    max_new_tokens: int | None = None,
+    q_out: torch.Tensor | None = None,
+    err: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """QK-RMSNorm + RoPE on q and k, then k and v appended to their pages, in
+    one kernel; returns the normalised, rotated q (``[B, Hq, T, D]``).
+
+    Equals ``apply_rope(q_norm(q), cos, sin)``, ``apply_rope(k_norm(k), cos,
+    sin)`` and ``append_only(k, v)`` of the reference
+    (src/barellm/models/attention.py:161-169, models/norm.py:14-21,
+    models/rope.py:53-68, engine/paged_kv_cache.py:151-193), with the same
+    roundings to the element type.  ``q``/``key``/``value``: ``[B, H, T, D]``
+    (any strides, D contiguous), or packed ``[1, H, sum T, D]`` with
+    ``new_offsets``.  ``cos``/``sin``: ``[B or 1, 1, T, D]`` as the reference's
+    RotaryEmbedding returns them (packed: ``[1, 1, sum T, D]``).
+    """
+    pl = _paged_layer(key_cache, value_cache, layer, block_tables, row_ids)
+    _check(q.ndim == 4 and key.ndim == 4 and value.ndim == 4, "q/K/V must have shape [B, H, T, D]")
+    _check(key.shape == value.shape, "K/V must have identical shape")
+    _check(key.shape[1] == key_cache.shape[2], "KV-head count cannot change")
+    _check(key.shape[2] > 0, "K/V sequence length must be greater than zero")
+    _check(key.shape[3] == key_cache.shape[4] and q.shape[3] == key.shape[3], "Head dimension cannot change")
+    _check(q.shape[0] == key.shape[0] and q.shape[2] == key.shape[2], "q and K/V must cover the same tokens")
+    _check(q.shape[1] % key.shape[1] == 0, "num_heads must divide evenly by num_kv_heads")
+    for t, name in ((q, "q"), (key, "K"), (value, "V"), (q_norm_weight, "q_norm_weight"),
+                    (k_norm_weight, "k_norm_weight"), (cos, "cos"), (sin, "sin")):
+        _check(t.dtype == key_cache.dtype, f"{name} dtype must match the K/V pool")
+        _check(t.device == key_cache.device, f"{name} must be on {key_cache.device}")
+        _check(t.stride(-1) == 1, f"{name} must have a contiguous last dimension")
+    d = key.shape[3]
+    _check(q_norm_weight.shape == (d,) and k_norm_weight.shape == (d,), "norm weights must have shape [head_dim]")
+    _check(cos.shape == sin.shape and cos.stride() == sin.stride(), "cos/sin must have identical shapes and strides")
+    _check(cos.ndim == 4 and cos.shape[1] == 1 and cos.shape[2] == q.shape[2] and cos.shape[3] == d,
+           "cos/sin must have shape [B or 1, 1, T, D]")
+    _check(cos.shape[0] in (1, q.shape[0]), "cos/sin batch must be 1 or B")
+    _int32_on(start_pos, key.device, "start_pos")
+    batch = start_pos.shape[0]
+    if new_offsets is None:
+        _check(key.shape[0] == batch, "batch size must match number of caches")
+        max_new = key.shape[2]
+    else:
+        _int32_on(new_offsets, key.device, "new_offsets")
+        _check(key.shape[0] == 1 and new_offsets.shape[0] == batch + 1, "packed K/V need [1, H, T, D] and [B+1] offsets")
+        _check(max_new_tokens is not None and max_new_tokens > 0, "packed append needs max_new_tokens")
+        max_new = int(max_new_tokens)
+    if q_out is None:
+        q_out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    _check(q_out.shape == q.shape and q_out.stride(3) == 1 and q_out.dtype == q.dtype, "q_out must match q")
+    a = nat.QkPrepArgs()
+    a.kv = pl
+    a.q_in, a.k_in, a.v_in, a.q_out = q.data_ptr(), key.data_ptr(), value.data_ptr(), q_out.data_ptr()
+    a.q_in_stride_b, a.q_in_stride_h, a.q_in_stride_t = q.stride(0), q.stride(1), q.stride(2)
+    a.k_in_stride_b, a.k_in_stride_h, a.k_in_stride_t = key.stride(0), key.stride(1), key.stride(2)
+    a.v_in_stride_b, a.v_in_stride_h, a.v_in_stride_t = value.stride(0), value.stride(1), value.stride(2)
+    a.q_out_stride_b, a.q_out_stride_h, a.q_out_stride_t = q_out.stride(0), q_out.stride(1), q_out.stride(2)
+    a.q_norm_weight, a.k_norm_weight = q_norm_weight.data_ptr(), k_norm_weight.data_ptr()
+    a.cos, a.sin = cos.data_ptr(), sin.data_ptr()
+    a.rope_stride_b = cos.stride(0) if cos.shape[0] > 1 else 0
+    a.rope_stride_t = cos.stride(2)
+    a.eps = float(eps)
+    a.num_q_heads = q.shape[1]
+    a.start_pos = start_pos.data_ptr()
+    a.new_offsets = _ptr(new_offsets)
+    a.batch = batch
+    a.max_new_tokens = max_new
+    a.err = _ptr(err)
+    _raise_rc(nat.load().bl_qk_norm_rope_append(a, _stream(key.device)))
+    return q_out
+
+
 def paged_gather(
     key_cache: torch.Tensor,
     value_cache: torch.Tensor,

@@ -283,6 +283,21 @@ class PagedLayerKV:
                          _i32([start], s.device), key, value, row_ids=_i32([req.row], s.device), err=s.err)
         req.layer_seq_lens[self.layer_idx] = start + key.shape[2]
 
+    def append_only_prepped(self, q: torch.Tensor, key: torch.Tensor, value: torch.Tensor, q_norm_weight,
+                            k_norm_weight, cos, sin, eps: float) -> torch.Tensor:
+        """append_only of the QK-normalised, rotated key, with the same norm and
+        rotation applied to ``q``, in one kernel; returns the prepared q."""
+        self.check_new_kv(key, value)
+        self.check_capacity(key.shape[2])
+        s = self.storage
+        req = self._request
+        start = int(req.layer_seq_lens[self.layer_idx])
+        q_out = ops.qk_norm_rope_append(q, key, value, q_norm_weight, k_norm_weight, cos, sin, eps, s.key_cache,
+                                        s.value_cache, self.layer_idx, s.arena.table, _i32([start], s.device),
+                                        row_ids=_i32([req.row], s.device), err=s.err)
+        req.layer_seq_lens[self.layer_idx] = start + key.shape[2]
+        return q_out
+
     def paged_metadata_post_append(self) -> PagedKVMetadata:
         check(self.seq_len > 0, "KV cache is empty")
         s = self.storage

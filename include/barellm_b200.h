@@ -119,6 +119,56 @@ typedef struct bl_append_args {
 BL_API int bl_paged_append(const bl_append_args* args, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* Fused QK-RMSNorm + RoPE + append: the per-layer step before attention.    */
+/* Replaces the reference's                                                  */
+/*   q = apply_rope(q_norm(q), cos, sin); k = apply_rope(k_norm(k), cos, sin) */
+/* (src/barellm/models/attention.py:161-169, models/norm.py:14-21,           */
+/* models/rope.py:53-68) followed by PagedLayerKV.append_only of k and v     */
+/* (src/barellm/engine/paged_kv_cache.py:151-193).  Writes the normalised,   */
+/* rotated q to q_out (q_in's layout, own strides) and the rotated k         */
+/* and the raw v into their pool slots (slot of token t of request b =       */
+/* start_pos[b] + t, as bl_paged_append).  Inputs are [B, H, T, D] with any  */
+/* strides and D contiguous, or packed [1, H, sum T, D] with new_offsets.    */
+/* cos / sin: [B or 1, T, D] element rows at b * rope_stride_b +             */
+/* token * rope_stride_t (token = packed index when new_offsets is given).   */
+/* Weights: [D], element type.  head_dim 64, 128 or 256.                     */
+typedef struct bl_qk_prep_args {
+  bl_paged_layer kv;
+  const void* q_in;
+  int64_t q_in_stride_b;
+  int64_t q_in_stride_h;
+  int64_t q_in_stride_t;
+  const void* k_in;
+  int64_t k_in_stride_b;
+  int64_t k_in_stride_h;
+  int64_t k_in_stride_t;
+  const void* v_in;
+  int64_t v_in_stride_b;
+  int64_t v_in_stride_h;
+  int64_t v_in_stride_t;
+  void* q_out;
+  int64_t q_out_stride_b;
+  int64_t q_out_stride_h;
+  int64_t q_out_stride_t;
+  const void* q_norm_weight;
+  const void* k_norm_weight;
+  const void* cos;
+  const void* sin;
+  int64_t rope_stride_b;
+  int64_t rope_stride_t;
+  float eps;
+  int32_t pad0;
+  int64_t num_q_heads;
+  const int32_t* start_pos;   /* [batch], device */
+  const int32_t* new_offsets; /* [batch+1], device, or NULL */
+  int64_t batch;
+  int64_t max_new_tokens;
+  int32_t* err;               /* device int32 or NULL */
+} bl_qk_prep_args;
+
+BL_API int bl_qk_norm_rope_append(const bl_qk_prep_args* args, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* Gather: dense read of pages, with optional zero padding.                  */
 /* Replaces PagedLayerKV.read (src/barellm/engine/paged_kv_cache.py:215-240) */
 /* and BatchLayerKV.read/_pad (src/barellm/engine/batched_kv_cache.py:65-95).*/

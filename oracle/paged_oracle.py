@@ -150,6 +150,38 @@ def prefill_attention(q, key_cache, value_cache, layer, block_table, seq_len, sc
     return sdpa(q, repeat_kv(k, group), repeat_kv(v, group), attn_mask=mask, scale=scale)
 
 
+def _identity(x):
+    return x
+
+
+def rms_norm(x, weight, eps: float, round_fn=None) -> np.ndarray:
+    """RMSNorm over the last axis; models/norm.py:14-21 (mean square, rsqrt
+    and the weight in float; one rounding to the element type at the end)."""
+    rnd = round_fn or _identity
+    xf = np.asarray(x, dtype=np.float64)
+    ms = np.mean(xf * xf, axis=-1, keepdims=True)
+    return rnd(xf / np.sqrt(ms + eps) * np.asarray(weight, dtype=np.float64))
+
+
+def rotate_half(x: np.ndarray) -> np.ndarray:
+    """models/rope.py:53-60: cat(-x[..., D/2:], x[..., :D/2])."""
+    half = x.shape[-1] // 2
+    return np.concatenate((-x[..., half:], x[..., :half]), axis=-1)
+
+
+def apply_rope(x, cos, sin, round_fn=None) -> np.ndarray:
+    """models/rope.py:63-68: x * cos + rotate_half(x) * sin, each tensor op
+    rounded to the element type (``round_fn``)."""
+    rnd = round_fn or _identity
+    x = np.asarray(x, dtype=np.float64)
+    return rnd(rnd(x * cos) + rnd(rotate_half(x) * sin))
+
+
+def qk_norm_rope(x, weight, cos, sin, eps: float, round_fn=None) -> np.ndarray:
+    """apply_rope(norm(x), cos, sin); models/attention.py:161-169."""
+    return apply_rope(rms_norm(x, weight, eps, round_fn), cos, sin, round_fn)
+
+
 def decode_attention_rows(q, k_rows, v_rows, scale=None):
     """Decode attention from per-row dense histories (the pool already gathered).
 

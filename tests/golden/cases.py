@@ -158,3 +158,78 @@ def decode_case(name: str) -> DecodeCase:
 def prefill_case(name: str) -> PrefillCase:
     seed, hq, hkv, d, bs, p, prefix, chunk = PREFILL_CASES[name]
     return make_prefill_case(seed, hq, hkv, d, bs, p, prefix, chunk)
+
+
+# ---------------------------------------------------------------------------
+# QK-RMSNorm + RoPE + append (the step before the attention)
+# ---------------------------------------------------------------------------
+@dataclass
+class QkPrepCase:
+    num_q_heads: int
+    num_kv_heads: int
+    head_dim: int
+    block_size: int
+    num_blocks: int
+    eps: float
+    theta: float
+    starts: np.ndarray     # [B] cached tokens before this step
+    free_ids: np.ndarray
+    q: np.ndarray          # [B, Hq, T, D] projections before the norm
+    k: np.ndarray          # [B, Hkv, T, D]
+    v: np.ndarray
+    q_weight: np.ndarray   # [D]
+    k_weight: np.ndarray
+
+    @property
+    def batch(self) -> int:
+        return self.q.shape[0]
+
+    @property
+    def new_tokens(self) -> int:
+        return self.q.shape[2]
+
+    def positions(self) -> np.ndarray:
+        return self.starts[:, None] + np.arange(self.new_tokens)[None, :]
+
+    def block_tables(self) -> list[np.ndarray]:
+        free = list(int(x) for x in self.free_ids)
+        out = []
+        for s in self.starts:
+            need = (int(s) + self.new_tokens + self.block_size - 1) // self.block_size
+            out.append(np.array([free.pop() for _ in range(need)], dtype=np.int64))
+        return out
+
+    def checksum(self) -> float:
+        return float(sum(np.abs(x).sum() for x in (self.q, self.k, self.v, self.q_weight, self.k_weight)))
+
+
+def make_qk_prep_case(seed: int, batch: int, num_q_heads: int, num_kv_heads: int, head_dim: int, block_size: int,
+                      num_blocks: int, new_tokens: int, max_start: int) -> QkPrepCase:
+    rs = np.random.RandomState(seed)
+    starts = rs.randint(0, max_start + 1, size=batch).astype(np.int64)
+    free_ids = rs.permutation(num_blocks).astype(np.int64)
+
+    def randn(*shape, scale=1.0):
+        return (rs.standard_normal(shape) * scale).astype(np.float32)
+
+    return QkPrepCase(num_q_heads, num_kv_heads, head_dim, block_size, num_blocks, 1e-6, 1_000_000.0, starts,
+                      free_ids, randn(batch, num_q_heads, new_tokens, head_dim, scale=2.0),
+                      randn(batch, num_kv_heads, new_tokens, head_dim, scale=2.0),
+                      randn(batch, num_kv_heads, new_tokens, head_dim),
+                      (1.0 + 0.1 * rs.standard_normal(head_dim)).astype(np.float32),
+                      (1.0 + 0.1 * rs.standard_normal(head_dim)).astype(np.float32))
+
+
+QK_PREP_CASES = {
+    # name: (seed, B, Hq, Hkv, D, bs, P, T, max_start)
+    "qk_prep_tiny": (31, 2, 4, 2, 64, 4, 64, 3, 20),
+    # Qwen3-0.6B attention shapes: one decode token per request, long positions
+    "qk_prep_qwen06b_decode": (32, 5, 16, 8, 128, 16, 4096, 1, 12000),
+    # Qwen3-8B attention shapes: a short prefill chunk over a prefix
+    "qk_prep_qwen8b_chunk": (33, 2, 32, 8, 128, 16, 512, 19, 300),
+}
+
+
+def qk_prep_case(name: str) -> QkPrepCase:
+    seed, b, hq, hkv, d, bs, p, t, max_start = QK_PREP_CASES[name]
+    return make_qk_prep_case(seed, b, hq, hkv, d, bs, p, t, max_start)

@@ -33,6 +33,8 @@ from barellm.engine.block_pool import BlockPool  # noqa: E402
 from barellm.engine.kv_cache_manager import KVCacheManager  # noqa: E402
 from barellm.engine.paged_kv_cache import PagedKVCache  # noqa: E402
 from barellm.engine.request import Request  # noqa: E402
+from barellm.models.norm import RMSNorm  # noqa: E402
+from barellm.models.rope import RotaryEmbedding, apply_rope  # noqa: E402
 
 SENTINEL = -7.0  # pool fill so untouched slots are known
 
@@ -210,9 +212,40 @@ def gen_batch_read() -> None:
     print("batch_read", tables.shape)
 
 
+def run_qk_prep(case: cases.QkPrepCase, dtype: torch.dtype) -> dict:
+    """The reference's QK-norm + RoPE (models/attention.py:161-169) on the case."""
+    d = case.head_dim
+    q_norm = RMSNorm(d, eps=case.eps)
+    k_norm = RMSNorm(d, eps=case.eps)
+    with torch.no_grad():
+        q_norm.weight.copy_(t(case.q_weight))
+        k_norm.weight.copy_(t(case.k_weight))
+    q_norm, k_norm = q_norm.to(dtype), k_norm.to(dtype)
+    rope = RotaryEmbedding(d, theta=case.theta)
+    q, k = t(case.q, dtype), t(case.k, dtype)
+    with torch.no_grad():
+        cos, sin = rope(q, torch.from_numpy(case.positions()))
+        q_out = apply_rope(q_norm(q), cos, sin)
+        k_out = apply_rope(k_norm(k), cos, sin)
+    return {"q_out": f32(q_out), "k_out": f32(k_out), "cos": f32(cos), "sin": f32(sin),
+            "q_weight": f32(q_norm.weight), "k_weight": f32(k_norm.weight)}
+
+
+def gen_qk_prep() -> None:
+    for name in cases.QK_PREP_CASES:
+        case = cases.qk_prep_case(name)
+        out = {}
+        for tag, dtype in (("f32", torch.float32), ("bf16", torch.bfloat16)):
+            for key, val in run_qk_prep(case, dtype).items():
+                out[f"{key}_{tag}"] = val
+        np.savez_compressed(HERE / f"{name}.npz", checksum=case.checksum(), **out)
+        print(name, out["q_out_f32"].shape)
+
+
 if __name__ == "__main__":
     torch.manual_seed(0)
     gen_storage_sequence()
     gen_batch_read()
     gen_decode()
     gen_prefill()
+    gen_qk_prep()

@@ -141,3 +141,33 @@ def test_decode_rows_helper_matches_padded_oracle():
     rows_k = [orc.read(kc, vc, 0, bt, n)[0][0] for bt, n in zip(tables, lens)]
     rows_v = [orc.read(kc, vc, 0, bt, n)[1][0] for bt, n in zip(tables, lens)]
     np.testing.assert_allclose(orc.decode_attention_rows(case.q[:, :, 0], rows_k, rows_v), out, atol=1e-12)
+
+
+@pytest.mark.parametrize("name", list(cases.QK_PREP_CASES))
+def test_qk_norm_rope_oracle_matches_reference(name):
+    g = load(name)
+    case = cases.qk_prep_case(name)
+    assert np.isclose(case.checksum(), float(g["checksum"]), rtol=1e-12), "seeded inputs drifted"
+    # float32: the float64 restatement on the reference's own cos/sin tables
+    q32 = orc.qk_norm_rope(case.q, g["q_weight_f32"], g["cos_f32"], g["sin_f32"], case.eps)
+    k32 = orc.qk_norm_rope(case.k, g["k_weight_f32"], g["cos_f32"], g["sin_f32"], case.eps)
+    np.testing.assert_allclose(q32, g["q_out_f32"], atol=1e-5, rtol=1e-5)
+    np.testing.assert_allclose(k32, g["k_out_f32"], atol=1e-5, rtol=1e-5)
+    # bf16: the same steps with each tensor op's rounding; the mean square's
+    # summation order may move a rare normalised element by one bf16 step,
+    # which RoPE carries as one step of x * cos or rotate_half(x) * sin
+    for src, key in ((case.q, "q"), (case.k, "k")):
+        rnd = lambda a: bf16_round(a.astype(np.float32))  # noqa: E731
+        out = orc.qk_norm_rope(bf16_round(src), g[f"{key}_weight_bf16"], g["cos_bf16"], g["sin_bf16"], case.eps,
+                               round_fn=rnd)
+        ref = g[f"{key}_out_bf16"]
+        assert_bf16_rope_close(out, ref, orc.rms_norm(bf16_round(src), g[f"{key}_weight_bf16"], case.eps, rnd),
+                               g["cos_bf16"], g["sin_bf16"])
+
+
+def assert_bf16_rope_close(out, ref, normed, cos, sin):
+    """All but a rare element equal; the rest within one bf16 step of the RoPE
+    products they came from."""
+    exact = np.mean(out == ref)
+    step = 2.0 ** -7 * (np.abs(normed * cos) + np.abs(orc.rotate_half(normed) * sin) + np.abs(ref)) + 1e-30
+    assert exact >= 0.99 and np.all(np.abs(out - ref) <= step), (exact, np.max(np.abs(out - ref)))
