@@ -14,6 +14,8 @@ with one scatter kernel and attends straight from the pages:
   * PagedLayerKV (single-request prefill, engine.py:226-257, including a
     non-empty prefix = chunked prefill): append, then paged prefill with the
     bottom-right causal mask (equal to SDPA(is_causal=True) without a prefix);
+  * PackedBatchLayerKV (batched chunked prefill: many requests' ragged chunks
+    packed on the token axis): one packed append, one paged prefill;
   * None (uncached full forward): the new K/V are paged into a scratch pool
     and attended causally by the same prefill kernel.
 There is no CPU path: a CPU tensor or an unknown cache type raises.
@@ -26,7 +28,7 @@ from typing import Literal, Protocol
 import torch
 
 from . import ops
-from .batched_kv_cache import BatchLayerKV
+from .batched_kv_cache import BatchLayerKV, PackedBatchLayerKV
 from .paged_kv_cache import PagedLayerKV, _i32, check
 
 AttentionBackendName = Literal["auto", "sdpa", "triton", "cuda"]
@@ -48,6 +50,8 @@ class CudaPagedAttentionBackend:
             return self._batched(q, new_k, new_v, layer_cache)
         if isinstance(layer_cache, PagedLayerKV):
             return self._single(q, new_k, new_v, layer_cache)
+        if isinstance(layer_cache, PackedBatchLayerKV):
+            return self._packed_attend(q, layer_cache, layer_cache.append_only(new_k, new_v))
         if layer_cache is None:
             return self._uncached(q, new_k, new_v)
         raise TypeError(f"the cuda attention backend reads paged caches, not {type(layer_cache).__name__}")
@@ -68,6 +72,9 @@ class CudaPagedAttentionBackend:
             check(q.shape[0] == 1, "PagedKVCache currently supports batch size 1")
             qp = layer_cache.append_only_prepped(q, new_k, new_v, q_norm_weight, k_norm_weight, cos, sin, eps)
             return self._single_attend(qp, layer_cache)
+        if isinstance(layer_cache, PackedBatchLayerKV):
+            meta, qp = layer_cache.append_only_prepped(q, new_k, new_v, q_norm_weight, k_norm_weight, cos, sin, eps)
+            return self._packed_attend(qp, layer_cache, meta)
         raise TypeError("fused QK preparation needs a paged cache; use attend() with prepared q/k")
 
     def _batched(self, q, new_k, new_v, layer: BatchLayerKV) -> torch.Tensor:
@@ -106,6 +113,13 @@ class CudaPagedAttentionBackend:
             return out.unsqueeze(2)
         return ops.paged_prefill(q, s.key_cache, s.value_cache, layer.layer_idx, s.arena.table, seq, row_ids=rows,
                                  err=s.err)
+
+    def _packed_attend(self, q, layer: PackedBatchLayerKV, meta) -> torch.Tensor:
+        """Chunked prefill of a packed batch: each row's chunk attends over its
+        cached prefix and itself (bottom-right causal), one kernel."""
+        s = layer.owner.storage
+        return ops.paged_prefill(q, s.key_cache, s.value_cache, layer.layer_idx, s.arena.table, meta.seq_lens,
+                                 q_offsets=meta.offsets, max_q_len=meta.max_chunk, row_ids=meta.rows, err=s.err)
 
     def _uncached(self, q, new_k, new_v) -> torch.Tensor:
         """Causal self-attention of a fresh sequence: page it into a scratch

@@ -247,3 +247,102 @@ class BatchLayerKV:
         tables.masked_fill_(col >= limit, -1)
         return PagedBatchKVMetadata(s.key_cache, s.value_cache, self.layer_idx, tables, meta.seq_lens.clone(),
                                     s.block_size)
+
+
+class PackedBatchKVCache:
+    """Several requests appending a ragged run of tokens each (batched,
+    chunked prefill), packed on the token axis: row b's ``chunk_lens[b]`` new
+    tokens are tokens ``offsets[b] .. offsets[b+1]`` of a ``[1, H, sum, D]``
+    tensor.  The reference prefills one request per forward with an empty
+    cache (src/barellm/engine/engine.py:187-310); this view lets one forward
+    prefill many requests, each continuing from whatever its cache already
+    holds (a chunk of a long prompt over its earlier chunks).
+
+    Every layer of one forward appends the same runs, so the device metadata
+    (arena rows, offsets, pre- and post-append lengths) is built once and
+    shared by all layers."""
+
+    def __init__(self, caches: list[PagedKVCacheView], chunk_lens: list[int]) -> None:
+        check(len(caches) > 0 and len(caches) == len(chunk_lens), "one chunk length per request")
+        check(all(n > 0 for n in chunk_lens), "K/V sequence length must be greater than zero")
+        storage = caches[0].storage
+        if not all(isinstance(c, PagedKVCacheView) and c.storage is storage for c in caches):
+            raise TypeError("packed prefill requires PagedKVCacheView members sharing one PagedKVCache")
+        self.caches = caches
+        self.storage = storage
+        pages = storage.request_pages
+        self.rows = np.fromiter((pages[c.request_id].row for c in caches), dtype=np.int64, count=len(caches))
+        self.chunk_lens = np.asarray(chunk_lens, dtype=np.int64)
+        self.total = int(self.chunk_lens.sum())
+        self.max_chunk = int(self.chunk_lens.max())
+        self._meta: PackedStepMeta | None = None
+
+    def layer(self, layer_idx: int) -> "PackedBatchLayerKV":
+        if not 0 <= layer_idx < self.storage.num_layers:
+            raise IndexError(f"Invalid layer index: {layer_idx}")
+        return PackedBatchLayerKV(self, layer_idx)
+
+    def step_meta(self, starts: np.ndarray) -> "PackedStepMeta":
+        if self._meta is None or not np.array_equal(self._meta.starts_host, starts):
+            self._meta = PackedStepMeta(self.storage, self.rows, starts, self.chunk_lens)
+        return self._meta
+
+
+class PackedStepMeta:
+    """Device metadata of one packed step: rows, pre-append lengths,
+    post-append lengths and token offsets, moved in one pinned copy."""
+
+    def __init__(self, storage: PagedKVCache, rows: np.ndarray, starts: np.ndarray, chunk_lens: np.ndarray) -> None:
+        b = len(rows)
+        host = torch.empty((4, b + 1), dtype=torch.int32)
+        if storage.device.type == "cuda":
+            host = host.pin_memory()
+        h = host.numpy()
+        h[0, :b] = rows
+        h[1, :b] = starts
+        h[2, :b] = starts + chunk_lens
+        h[3, 0] = 0
+        h[3, 1:] = np.cumsum(chunk_lens)
+        dev = host.to(storage.device, non_blocking=True)
+        self._host, self._dev = host, dev
+        self.rows, self.starts, self.seq_lens, self.offsets = dev[0, :b], dev[1, :b], dev[2, :b], dev[3]
+        self.starts_host = np.array(starts, dtype=np.int64)
+        self.max_chunk = int(chunk_lens.max())
+
+
+class PackedBatchLayerKV:
+    """One layer of a PackedBatchKVCache."""
+
+    def __init__(self, owner: PackedBatchKVCache, layer_idx: int) -> None:
+        self.owner = owner
+        self.layer_idx = int(layer_idx)
+
+    def _begin(self, key: torch.Tensor, value: torch.Tensor) -> tuple[PagedKVCache, np.ndarray, PackedStepMeta]:
+        o = self.owner
+        s = o.storage
+        check(key.ndim == 4 and key.shape[0] == 1 and key.shape[2] == o.total,
+              "packed K/V must have shape [1, H, sum of chunk lengths, D]")
+        check(value.shape == key.shape, "K/V must have identical shape")
+        s.check_new_kv(key, value, batch=1)
+        starts = s.arena.lens[o.rows, self.layer_idx]
+        ends = starts + o.chunk_lens
+        need = (ends + s.block_size - 1) // s.block_size
+        check(bool((need <= s.arena.used[o.rows]).all()), "request does not have enough allocated KV blocks")
+        return s, ends, o.step_meta(starts)
+
+    def append_only(self, key: torch.Tensor, value: torch.Tensor) -> PackedStepMeta:
+        s, ends, meta = self._begin(key, value)
+        ops.paged_append(s.key_cache, s.value_cache, self.layer_idx, s.arena.table, meta.starts, key, value,
+                         row_ids=meta.rows, new_offsets=meta.offsets, max_new_tokens=meta.max_chunk, err=s.err)
+        s.arena.lens[self.owner.rows, self.layer_idx] = ends
+        return meta
+
+    def append_only_prepped(self, q: torch.Tensor, key: torch.Tensor, value: torch.Tensor, q_norm_weight,
+                            k_norm_weight, cos, sin, eps: float) -> tuple[PackedStepMeta, torch.Tensor]:
+        s, ends, meta = self._begin(key, value)
+        q_out = ops.qk_norm_rope_append(q, key, value, q_norm_weight, k_norm_weight, cos, sin, eps, s.key_cache,
+                                        s.value_cache, self.layer_idx, s.arena.table, meta.starts,
+                                        row_ids=meta.rows, new_offsets=meta.offsets, max_new_tokens=meta.max_chunk,
+                                        err=s.err)
+        s.arena.lens[self.owner.rows, self.layer_idx] = ends
+        return meta, q_out

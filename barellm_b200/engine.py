@@ -16,12 +16,13 @@ from __future__ import annotations
 import math
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 import torch.nn.functional as F
 from torch import nn
 
 from .backend import CudaPagedAttentionBackend
-from .batched_kv_cache import BatchKVCache
+from .batched_kv_cache import BatchKVCache, PackedBatchKVCache
 from .block_pool import BlockPool
 from .kv_cache_manager import KVCacheManager
 from .paged_kv_cache import PagedKVCache
@@ -136,11 +137,16 @@ class Qwen3(nn.Module):
         for blk in self.layers:
             blk.self_attn.backend = backend
 
-    def forward(self, token_ids: torch.Tensor, position_ids: torch.Tensor, kv_cache=None) -> torch.Tensor:
+    def forward(self, token_ids: torch.Tensor, position_ids: torch.Tensor, kv_cache=None,
+                logits_index: torch.Tensor | None = None) -> torch.Tensor:
+        """``logits_index``: token positions (on the T axis) whose logits are
+        wanted; the LM head then runs on those rows only."""
         h = self.embed[token_ids]
         cos, sin = rope_cos_sin(self.s.head_dim, self.s.rope_theta, position_ids, h.dtype)
         for i, blk in enumerate(self.layers):
             h = blk(h, cos, sin, None if kv_cache is None else kv_cache.layer(i))
+        if logits_index is not None:
+            h = h[:, logits_index]
         return torch.matmul(self.norm(h), self.embed.T)
 
 
@@ -161,14 +167,45 @@ class _Request:
         return len(self.tokens)
 
 
+def plan_prefill_chunks(prompt_lens: list[int], budget: int) -> list[list[tuple[int, int, int]]]:
+    """Groups of (request, first token, token count) runs, each group at most
+    ``budget`` tokens, taking prompts in order and splitting a prompt where a
+    group's budget ends (its remainder opens the next group)."""
+    check_positive = budget > 0 and all(n > 0 for n in prompt_lens)
+    if not check_positive:
+        raise ValueError("prefill budget and prompt lengths must be positive")
+    groups: list[list[tuple[int, int, int]]] = []
+    group: list[tuple[int, int, int]] = []
+    left = budget
+    for r, n in enumerate(prompt_lens):
+        s = 0
+        while s < n:
+            take = min(n - s, left)
+            group.append((r, s, take))
+            s += take
+            left -= take
+            if left == 0:
+                groups.append(group)
+                group, left = [], budget
+    if group:
+        groups.append(group)
+    return groups
+
+
 class PagedEngine:
     """Prefill-then-batched-greedy-decode over a paged cache on one GPU.
 
-    Each request is prefilled on its own (as the reference engine does, through
-    the single-request PagedLayerKV path, engine.py:226-257); every decode step
-    then runs all requests as one BatchKVCache batch (engine.py:458-488)."""
+    Prefill packs the prompts of many requests into one forward of at most
+    ``prefill_tokens`` tokens, splitting a long prompt into chunks that each
+    continue over the request's cached earlier chunks (PackedBatchKVCache; the
+    reference prefills one request per forward, engine.py:226-257, and has no
+    chunked prefill, docs/ROADMAP.md:131).  ``prefill_tokens=0`` prefills each
+    request on its own through the single-request PagedLayerKV path, as the
+    reference does.  Every decode step then runs all requests as one
+    BatchKVCache batch (engine.py:458-488)."""
 
-    def __init__(self, model: Qwen3, num_blocks: int, block_size: int = 16, max_requests: int = 256) -> None:
+    def __init__(self, model: Qwen3, num_blocks: int, block_size: int = 16, max_requests: int = 256,
+                 prefill_tokens: int = 8192) -> None:
         s = model.s
         dev = next(model.parameters()).device
         dtype = next(model.parameters()).dtype
@@ -179,6 +216,7 @@ class PagedEngine:
         self.pool = BlockPool(num_blocks)
         self.manager = KVCacheManager(block_size, self.pool, self.cache)
         self.device = dev
+        self.prefill_tokens = int(prefill_tokens)
 
     @staticmethod
     def blocks_needed(prompt_lens: list[int], max_new: int, block_size: int) -> int:
@@ -200,10 +238,15 @@ class PagedEngine:
         for r in reqs:
             if not self.manager.allocate_request(r):
                 raise RuntimeError("KV pool exhausted during prefill")
-            ids = torch.tensor([r.tokens], dtype=torch.long, device=dev)
-            pos = torch.arange(r.seq_len, device=dev).unsqueeze(0)
-            logits = self.model(ids, pos, kv_cache=self.manager.get_cache(r))
-            r.tokens.append(int(torch.argmax(logits[0, -1]).item()))
+        if self.prefill_tokens > 0:
+            self._prefill_packed(reqs)
+        else:
+            for r in reqs:
+                ids = torch.tensor([r.tokens], dtype=torch.long, device=dev)
+                pos = torch.arange(r.seq_len, device=dev).unsqueeze(0)
+                last = torch.tensor([r.seq_len - 1], device=dev)
+                logits = self.model(ids, pos, kv_cache=self.manager.get_cache(r), logits_index=last)
+                r.tokens.append(int(torch.argmax(logits[0, -1]).item()))
         t1.record()
         if use_graph and max_new_tokens > 2:
             self._decode_graph(reqs, max_new_tokens - 1)
@@ -229,6 +272,25 @@ class PagedEngine:
         for r in reqs:
             self.manager.free_request(r.id)
         return out
+
+    def _prefill_packed(self, reqs: list[_Request]) -> None:
+        """One forward per group of ``plan_prefill_chunks``; a request's first
+        token comes from the forward holding its prompt's last token."""
+        dev = self.device
+        plens = [r.seq_len for r in reqs]
+        for group in plan_prefill_chunks(plens, self.prefill_tokens):
+            ids = np.concatenate([reqs[m].tokens[s:s + n] for m, s, n in group])
+            pos = np.concatenate([np.arange(s, s + n) for _, s, n in group])
+            ends = np.cumsum([n for _, _, n in group]) - 1
+            finishing = [k for k, (m, s, n) in enumerate(group) if s + n == plens[m]]
+            cache = PackedBatchKVCache([self.manager.get_cache(reqs[m]) for m, _, _ in group], [n for _, _, n in group])
+            ids_d = torch.from_numpy(ids.astype(np.int64)).to(dev, non_blocking=True).unsqueeze(0)
+            pos_d = torch.from_numpy(pos.astype(np.int64)).to(dev, non_blocking=True).unsqueeze(0)
+            idx_d = torch.from_numpy(ends[finishing].astype(np.int64)).to(dev, non_blocking=True)
+            logits = self.model(ids_d, pos_d, kv_cache=cache, logits_index=idx_d)
+            if finishing:
+                for k, tok in zip(finishing, torch.argmax(logits[0], dim=-1).tolist()):
+                    reqs[group[k][0]].tokens.append(int(tok))
 
     def _decode_graph(self, reqs: list[_Request], steps: int) -> None:
         dev = self.device

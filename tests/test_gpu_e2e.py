@@ -81,3 +81,19 @@ def test_bf16_qwen06b_attention_shapes_match_up_to_near_ties(cuda, native_lib):
         k = next(i for i, (a, b) in enumerate(zip(g, w)) if a != b)
         assert m[k] < 0.25, f"divergence at step {k} with oracle top-2 margin {m[k]:.3f}"
     assert identical >= len(prompts) // 2
+
+
+def test_fp32_packed_chunked_prefill_matches_per_request_prefill(cuda, native_lib):
+    """Batched prefill with a small token budget (prompts packed together and
+    long prompts split into chunks over their cached earlier chunks) gives the
+    same greedy tokens as one-request-per-forward prefill and as the
+    contiguous-cache oracle."""
+    shape = Qwen3Shape(vocab_size=512, hidden_size=256, intermediate_size=512, head_dim=64, num_layers=3,
+                       num_heads=4, num_kv_heads=2)
+    model = random_qwen3(shape, dtype=torch.float32, device=cuda, seed=21)
+    prompts = prompts_for(7, 3, 90, shape.vocab_size, seed=22)
+    blocks = PagedEngine.blocks_needed([len(p) for p in prompts], 10, 16) + 4
+    packed = PagedEngine(model, num_blocks=blocks, prefill_tokens=48).generate(prompts, max_new_tokens=10)
+    single = PagedEngine(model, num_blocks=blocks, prefill_tokens=0).generate(prompts, max_new_tokens=10)
+    want, _ = generate_contiguous(model, prompts, 10)
+    assert packed == single == want

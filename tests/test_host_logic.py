@@ -128,3 +128,22 @@ def test_backend_factory_names():
         create_attention_backend("triton")
     with pytest.raises(ValueError, match="Unknown attention backend"):
         create_attention_backend("flash")  # type: ignore[arg-type]
+
+
+def test_prefill_chunk_plan_packs_and_splits_prompts_in_order():
+    from barellm_b200.engine import plan_prefill_chunks
+
+    groups = plan_prefill_chunks([5, 3, 10, 2], 6)
+    assert groups == [[(0, 0, 5), (1, 0, 1)], [(1, 1, 2), (2, 0, 4)], [(2, 4, 6)], [(3, 0, 2)]]
+    assert all(sum(n for _, _, n in g) <= 6 for g in groups)
+    # every prompt token is covered exactly once, in order
+    for lens, budget in (([1] * 9, 4), ([17, 1, 33], 8), ([100], 7), ([3, 4, 5], 1000)):
+        seen = {}
+        for g in plan_prefill_chunks(lens, budget):
+            assert len({r for r, _, _ in g}) == len(g)  # a request appears once per group
+            for r, s, n in g:
+                assert s == seen.get(r, 0) and n > 0
+                seen[r] = s + n
+        assert [seen[r] for r in range(len(lens))] == lens
+    with pytest.raises(ValueError):
+        plan_prefill_chunks([3, 0], 4)
