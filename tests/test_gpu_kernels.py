@@ -242,7 +242,7 @@ def prefill_state(case: cases.PrefillCase, dtype, device):
 
 
 @pytest.mark.parametrize("name", list(cases.PREFILL_CASES))
-@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 def test_prefill_matches_oracle_and_reference(cuda, native_lib, name, dtype):
     case = cases.prefill_case(name)
     g = golden(name)
@@ -259,17 +259,19 @@ def test_prefill_matches_oracle_and_reference(cuda, native_lib, name, dtype):
         np.testing.assert_allclose(out, g["out_f32"], atol=F32_TOL, rtol=F32_TOL)
     else:
         assert_close_lowp(out, ref)
-        assert_close_lowp(out, g["out_bf16"])
+        if dtype == torch.bfloat16:
+            assert_close_lowp(out, g["out_bf16"])
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("hq,hkv", [(32, 8), (16, 8), (8, 8), (64, 8)])
-def test_packed_chunked_prefill_many_requests(cuda, native_lib, hq, hkv):
+def test_packed_chunked_prefill_many_requests(cuda, native_lib, hq, hkv, dtype):
     """Several requests with different prefixes and chunk lengths packed into
-    one call (q_offsets), bf16, tensor-core path; each row vs the fp64 oracle."""
+    one call (q_offsets), tensor-core path; each row vs the fp64 oracle."""
     rs = np.random.RandomState(hq)
     specs = [(0, 45), (37, 130), (300, 17), (16, 200), (513, 64)]
     bs, D, P = 16, 128, 512
-    kc = torch.full((1, P, hkv, bs, D), gh.SENTINEL, dtype=torch.bfloat16, device=cuda)
+    kc = torch.full((1, P, hkv, bs, D), gh.SENTINEL, dtype=dtype, device=cuda)
     vc = torch.full_like(kc, gh.SENTINEL)
     free = list(rs.permutation(P))
     tables, qs, lens = [], [], []
@@ -279,10 +281,10 @@ def test_packed_chunked_prefill_many_requests(cuda, native_lib, hq, hkv):
         lens.append(total)
     bt = torch.from_numpy(gh.padded_tables(tables)).to(cuda)
     for b, (prefix, chunk) in enumerate(specs):
-        k = torch.randn(1, hkv, prefix + chunk, D).to(torch.bfloat16).to(cuda)
-        v = torch.randn(1, hkv, prefix + chunk, D).to(torch.bfloat16).to(cuda)
+        k = torch.randn(1, hkv, prefix + chunk, D).to(dtype).to(cuda)
+        v = torch.randn(1, hkv, prefix + chunk, D).to(dtype).to(cuda)
         ops.paged_append(kc, vc, 0, bt[b : b + 1], torch.tensor([0], dtype=torch.int32, device=cuda), k, v)
-        qs.append(torch.randn(1, hq, chunk, D).to(torch.bfloat16).to(cuda))
+        qs.append(torch.randn(1, hq, chunk, D).to(dtype).to(cuda))
     q = torch.cat(qs, dim=2)
     offs = torch.tensor(np.concatenate([[0], np.cumsum([c for _, c in specs])]), dtype=torch.int32, device=cuda)
     seq = torch.tensor(lens, dtype=torch.int32, device=cuda)

@@ -22,7 +22,7 @@ from test_oracle_golden import assert_bf16_rope_close
 pytestmark = pytest.mark.gpu
 
 GOLDEN = cases.__file__.rsplit("/", 1)[0]
-TAG = {torch.float32: "f32", torch.bfloat16: "bf16"}
+TAG = {torch.float32: "f32", torch.bfloat16: "bf16", torch.float16: "f32"}  # fp16: the f32 tables, rounded
 
 
 def golden(name):
@@ -86,7 +86,7 @@ def run_case(name: str, dtype: torch.dtype, device, packed: bool = False):
 
 @pytest.mark.parametrize("packed", [False, True])
 @pytest.mark.parametrize("name", list(cases.QK_PREP_CASES))
-@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 def test_qk_prep_matches_reference(cuda, native_lib, name, dtype, packed):
     case, g, st, q_out = run_case(name, dtype, cuda, packed)
     tag = TAG[dtype]
@@ -97,10 +97,14 @@ def test_qk_prep_matches_reference(cuda, native_lib, name, dtype, packed):
     if dtype == torch.float32:
         np.testing.assert_allclose(q_out, g["q_out_f32"], atol=1e-5, rtol=1e-5)
         np.testing.assert_allclose(k_out, g["k_out_f32"], atol=1e-5, rtol=1e-5)
-    else:
-        for out, src, key in ((q_out, case.q, "q"), (k_out, case.k, "k")):
-            normed = orc.rms_norm(rnd(src), g[f"{key}_weight_{tag}"], case.eps, rnd)
-            assert_bf16_rope_close(out, g[f"{key}_out_{tag}"], normed, g[f"cos_{tag}"], g[f"sin_{tag}"])
+        return
+    cos, sin = rnd(g[f"cos_{tag}"]), rnd(g[f"sin_{tag}"])
+    for out, src, key in ((q_out, case.q, "q"), (k_out, case.k, "k")):
+        w = rnd(g[f"{key}_weight_{tag}"])
+        normed = orc.rms_norm(rnd(src), w, case.eps, rnd)
+        # bf16: the reference's own output; fp16: the oracle with fp16 rounding
+        want = g[f"{key}_out_bf16"] if dtype == torch.bfloat16 else orc.qk_norm_rope(rnd(src), w, cos, sin, case.eps, rnd)
+        assert_bf16_rope_close(out, want, normed, cos, sin)
 
 
 def test_qk_prep_leaves_other_slots_untouched(cuda, native_lib):
