@@ -86,11 +86,17 @@ class CudaPagedAttentionBackend:
         if q.shape[2] == 1:
             serial = ops.plan_serial(s.device)
             if meta.plan_ws is None or meta.plan_token != serial or meta.plan_heads != q.shape[1]:
-                # once per step: the plan depends only on the lengths, not the layer
-                meta.plan_ws = ops.paged_decode_plan(s.key_cache, s.value_cache, s.arena.table, meta.seq_lens,
-                                                     meta.max_seq_len, q.shape[1], row_ids=meta.rows, err=s.err)
+                # once per step (the plan depends only on the lengths, not the
+                # layer): plan + attention + reduce in one call, into the shared
+                # workspace that the step's later layers then reuse
+                ws = ops.workspace(s.device, ops.decode_workspace_bytes(q.shape[0], q.shape[1], q.shape[3],
+                                                                        s.block_size, meta.max_seq_len))
+                out = ops.paged_decode(q, s.key_cache, s.value_cache, idx, s.arena.table, meta.seq_lens,
+                                       meta.max_seq_len, row_ids=meta.rows, ws=ws, plan_ready=False, err=s.err)
+                meta.plan_ws = ws
                 meta.plan_token = ops.plan_serial(s.device)
                 meta.plan_heads = q.shape[1]
+                return out.unsqueeze(2)
             out = ops.paged_decode(q, s.key_cache, s.value_cache, idx, s.arena.table, meta.seq_lens,
                                    meta.max_seq_len, row_ids=meta.rows, ws=meta.plan_ws, plan_ready=True, err=s.err)
             return out.unsqueeze(2)

@@ -32,9 +32,7 @@ class StepMeta:
     def __init__(self, storage: PagedKVCache, rows: np.ndarray, starts: np.ndarray, new_tokens: int,
                  static_max_seq_len: int | None = None) -> None:
         b = len(rows)
-        host = torch.empty((3, b), dtype=torch.int32)
-        if storage.device.type == "cuda":
-            host = host.pin_memory()
+        host = torch.empty((3, b), dtype=torch.int32, pin_memory=storage.device.type == "cuda")
         self._host = host
         h = host.numpy()
         h[0] = rows
@@ -294,9 +292,7 @@ class PackedStepMeta:
 
     def __init__(self, storage: PagedKVCache, rows: np.ndarray, starts: np.ndarray, chunk_lens: np.ndarray) -> None:
         b = len(rows)
-        host = torch.empty((4, b + 1), dtype=torch.int32)
-        if storage.device.type == "cuda":
-            host = host.pin_memory()
+        host = torch.empty((4, b + 1), dtype=torch.int32, pin_memory=storage.device.type == "cuda")
         h = host.numpy()
         h[0, :b] = rows
         h[1, :b] = starts

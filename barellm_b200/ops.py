@@ -40,7 +40,14 @@ def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream(device: torch.device) -> int:
+    """The current CUDA stream of ``device`` as a raw handle (the fast
+    accessor when this torch build has it)."""
+    if _raw_stream is not None:
+        return _raw_stream(device.index if device.index is not None else torch.cuda.current_device())
     return torch.cuda.current_stream(device).cuda_stream
 
 
@@ -289,6 +296,7 @@ def decode_workspace_bytes(batch: int, num_q_heads: int, head_dim: int, block_si
 
 
 _WORKSPACES: dict[int, torch.Tensor] = {}
+_PLAN_STUBS: dict[tuple, torch.Tensor] = {}
 _PLAN_SERIAL: dict[int, int] = {}
 
 
@@ -389,9 +397,15 @@ def paged_decode_plan(
     """Builds the split-K plan for ``seq_lens`` once; reusable by every layer."""
     batch = seq_lens.shape[0]
     d = key_cache.shape[4]
-    q_dummy = torch.empty((batch, num_q_heads, d), dtype=key_cache.dtype, device=key_cache.device)
-    a, _, ws = _decode_args(q_dummy, key_cache, value_cache, 0, block_tables, seq_lens, max_seq_len, None,
-                            q_dummy, row_ids, ws, False, err)
+    # the plan reads no q / out: a broadcast [B, Hq, D] view of one cached
+    # D-element row stands in for them
+    key = (key_cache.device, key_cache.dtype, d)
+    row = _PLAN_STUBS.get(key)
+    if row is None:
+        row = _PLAN_STUBS[key] = torch.zeros(d, dtype=key_cache.dtype, device=key_cache.device)
+    q_shape = row.as_strided((batch, num_q_heads, d), (0, 0, 1))
+    a, _, ws = _decode_args(q_shape, key_cache, value_cache, 0, block_tables, seq_lens, max_seq_len, None,
+                            q_shape, row_ids, ws, False, err)
     _raise_rc(nat.load().bl_paged_decode_plan(a, _stream(key_cache.device)))
     idx = _dev_index(key_cache.device)
     if _WORKSPACES.get(idx) is ws:
