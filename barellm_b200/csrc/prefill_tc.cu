@@ -6,22 +6,23 @@
 // share one KV head, as two 128-row tiles A and B (head-major rows, so for
 // G >= 2 both tiles cover the same tokens and need the same keys).  Every K/V
 // page is fetched once for 256 rows, which halves the K/V bytes per flop of a
-// 128-row tile; keys are consumed in tiles of 128 (8 pages).  Warp roles:
-//   warps 0..1  producers: K and V pages of a key tile into 2-stage K and V
-//               rings, 16-byte cp.async per thread written in the 128-byte
-//               swizzled layout the MMA reads (paged 4 KB pages stream about
-//               four times faster this way than as 2 KB TMA boxes).  Each
-//               thread's copies arrive on the stage's mbarrier when they land;
-//               V of tile t-1 goes out before K of tile t (P V comes first).
-//               Slots past the row length or the row's last page are written
+// 128-row tile; keys are consumed in tiles of 128 (8 pages).  Warp roles (12 warps):
+//   warp 0      K producer (one lane): the 8 pages of key tile t as 2-D TMA
+//               boxes (64 x 16, 128-byte swizzle) into a 3-stage K ring; a
+//               page past the row's last page is read at an out-of-range row
+//               coordinate, which TMA fills with zeros.
+//   warps 1..2  V producers: the V pages of tile t-1 into a 2-stage V ring,
+//               16-byte cp.async per thread written in the 128-byte swizzled
+//               layout the MMA reads; slots past the row length are written
 //               as zeros (src-size 0), so stale pool bytes never reach P V.
-//   warp 2      TMEM owner (512 columns: S_A 0..127, S_B 128..255, O_A 256..383,
+//               Each thread's copies arrive on the stage's mbarrier (noinc).
+//   warp 3      TMEM owner (512 columns: S_A 0..127, S_B 128..255, O_A 256..383,
 //               O_B 384..511) and, on one lane, the MMA issuer.  Per key tile t
 //               it issues O_A += P_A V_{t-1}, S_A = Q_A K_t^T, O_B += P_B V_{t-1},
 //               S_B = Q_B K_t^T, so one tile's softmax runs while the tensor
 //               pipe works on the other tile.  S_X is rewritten only after the
 //               P V that read P_X (stored in S_X's columns) has completed.
-//   warps 3..6  softmax of tile A, warps 7..10 of tile B: one thread per score
+//   warps 4..7  softmax of tile A, warps 8..11 of tile B: one thread per score
 //               row (= TMEM lane).  The S row is read from TMEM once into
 //               registers (bottom-right causal mask, row max in log2 units),
 //               exponentiated and written back as packed bf16/fp16 P over the
