@@ -6,6 +6,7 @@ attention backend, backed by hand-written CUDA kernels behind a C ABI
 
     PagedKVCache / PagedKVCacheView / PagedLayerKV   paged_kv_cache.py
     BatchKVCache / BatchLayerKV                      batched_kv_cache.py
+    PackedBatchKVCache / PackedBatchLayerKV          batched_kv_cache.py (batched chunked prefill)
     BlockPool / KVCacheBlock, KVCacheManager         block_pool.py, kv_cache_manager.py
     CudaPagedAttentionBackend, create_attention_backend  backend.py
     ops (tensor-level kernel wrappers)                ops.py
@@ -13,7 +14,7 @@ attention backend, backed by hand-written CUDA kernels behind a C ABI
 
 from . import ops
 from .backend import AttentionBackendName, CudaPagedAttentionBackend, create_attention_backend
-from .batched_kv_cache import BatchKVCache, BatchLayerKV
+from .batched_kv_cache import BatchKVCache, BatchLayerKV, PackedBatchKVCache, PackedBatchLayerKV
 from .block_pool import BlockPool, KVCacheBlock
 from .kv_cache_manager import KVCacheManager
 from .paged_kv_cache import (
@@ -34,6 +35,8 @@ __all__ = [
     "CudaPagedAttentionBackend",
     "KVCacheBlock",
     "KVCacheManager",
+    "PackedBatchKVCache",
+    "PackedBatchLayerKV",
     "PagedBatchKVMetadata",
     "PagedKVCache",
     "PagedKVCacheView",

@@ -83,23 +83,24 @@ class CudaPagedAttentionBackend:
     def _batched_attend(self, q, layer: BatchLayerKV, meta) -> torch.Tensor:
         s = layer.storage()
         idx = layer.layer_idx
-        if q.shape[2] == 1:
+        b, hq, t, d = q.shape
+        if t == 1:
+            out = torch.empty((b, hq, 1, d), dtype=q.dtype, device=q.device)
             serial = ops.plan_serial(s.device)
-            if meta.plan_ws is None or meta.plan_token != serial or meta.plan_heads != q.shape[1]:
+            if meta.plan_ws is None or meta.plan_token != serial or meta.plan_heads != hq:
                 # once per step (the plan depends only on the lengths, not the
                 # layer): plan + attention + reduce in one call, into the shared
                 # workspace that the step's later layers then reuse
-                ws = ops.workspace(s.device, ops.decode_workspace_bytes(q.shape[0], q.shape[1], q.shape[3],
-                                                                        s.block_size, meta.max_seq_len))
-                out = ops.paged_decode(q, s.key_cache, s.value_cache, idx, s.arena.table, meta.seq_lens,
-                                       meta.max_seq_len, row_ids=meta.rows, ws=ws, plan_ready=False, err=s.err)
+                ws = ops.workspace(s.device, ops.decode_workspace_bytes(b, hq, d, s.block_size, meta.max_seq_len))
+                ops.paged_decode(q, s.key_cache, s.value_cache, idx, s.arena.table, meta.seq_lens, meta.max_seq_len,
+                                 out=out, row_ids=meta.rows, ws=ws, plan_ready=False, err=s.err)
                 meta.plan_ws = ws
                 meta.plan_token = ops.plan_serial(s.device)
-                meta.plan_heads = q.shape[1]
-                return out.unsqueeze(2)
-            out = ops.paged_decode(q, s.key_cache, s.value_cache, idx, s.arena.table, meta.seq_lens,
-                                   meta.max_seq_len, row_ids=meta.rows, ws=meta.plan_ws, plan_ready=True, err=s.err)
-            return out.unsqueeze(2)
+                meta.plan_heads = hq
+                return out
+            ops.paged_decode(q, s.key_cache, s.value_cache, idx, s.arena.table, meta.seq_lens, meta.max_seq_len,
+                             out=out, row_ids=meta.rows, ws=meta.plan_ws, plan_ready=True, err=s.err)
+            return out
         return ops.paged_prefill(q, s.key_cache, s.value_cache, idx, s.arena.table, meta.seq_lens,
                                  row_ids=meta.rows, err=s.err)
 

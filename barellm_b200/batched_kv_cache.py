@@ -14,11 +14,17 @@ reads are one kernel launch for the whole batch.
 
 from __future__ import annotations
 
+from operator import attrgetter
+
 import numpy as np
 import torch
 
 from . import ops
 from .paged_kv_cache import PagedBatchKVMetadata, PagedKVCache, PagedKVCacheView, PagedLayerKV, check
+
+
+_STORAGE = attrgetter("storage")
+_REQUEST_ID = attrgetter("request_id")
 
 
 class StepMeta:
@@ -37,9 +43,9 @@ class StepMeta:
         h = host.numpy()
         h[0] = rows
         h[1] = starts
-        h[2] = starts + new_tokens
+        np.add(starts, new_tokens, out=h[2], casting="unsafe")
         self._dev = host.to(storage.device, non_blocking=True)
-        self.rows, self.starts, self.seq_lens = self._dev[0], self._dev[1], self._dev[2]
+        self.rows, self.starts, self.seq_lens = self._dev.unbind(0)
         self.seq_lens_host = h[2].astype(np.int64)
         self.static = static_max_seq_len is not None
         self.max_seq_len = int(static_max_seq_len) if self.static else int(self.seq_lens_host.max())
@@ -85,15 +91,10 @@ class BatchKVCache:
         self._static: StepMeta | None = None
         first = getattr(caches[0], "storage", None)
         self.storage: PagedKVCache | None = None
-        if isinstance(first, PagedKVCache) and all(
-            isinstance(c, PagedKVCacheView) and c.storage is first for c in caches
-        ):
+        if (isinstance(first, PagedKVCache) and all(issubclass(t, PagedKVCacheView) for t in set(map(type, caches)))
+                and set(map(_STORAGE, caches)) == {first}):
             self.storage = first
-            pages = first.request_pages
-            try:
-                self.rows = np.fromiter((pages[c.request_id].row for c in caches), dtype=np.int64, count=len(caches))
-            except KeyError as exc:
-                raise KeyError(f"Unknown request: {exc.args[0]}") from exc
+            self.rows = first.rows_for(tuple(map(_REQUEST_ID, caches)))
             if static_max_seq_len is not None:
                 zeros = np.zeros(len(caches), dtype=np.int64)
                 self._static = StepMeta(first, self.rows, zeros, 0, static_max_seq_len=static_max_seq_len)
@@ -178,8 +179,8 @@ class BatchLayerKV:
         rows = self.owner.rows
         starts = s.arena.lens[rows, self.layer_idx]
         ends = starts + t
-        need = (ends + s.block_size - 1) // s.block_size
-        check(bool((need <= s.arena.used[rows]).all()), "request does not have enough allocated KV blocks")
+        # ceil(end / bs) <= blocks  <=>  end <= blocks * bs
+        check(bool((ends <= s.arena.used[rows] * s.block_size).all()), "request does not have enough allocated KV blocks")
         return s, rows, ends, self.owner.step_meta(starts, t)
 
     def append_only(self, key: torch.Tensor, value: torch.Tensor) -> StepMeta:
@@ -269,7 +270,7 @@ class PackedBatchKVCache:
         self.caches = caches
         self.storage = storage
         pages = storage.request_pages
-        self.rows = np.fromiter((pages[c.request_id].row for c in caches), dtype=np.int64, count=len(caches))
+        self.rows = storage.rows_for(tuple(map(_REQUEST_ID, caches)))
         self.chunk_lens = np.asarray(chunk_lens, dtype=np.int64)
         self.total = int(self.chunk_lens.sum())
         self.max_chunk = int(self.chunk_lens.max())

@@ -28,62 +28,85 @@ struct AppendKernelArgs {
   char* v_pool;
   const char* k_new;
   const char* v_new;
-  int64_t num_blocks, hkv, bs, row_bytes, layer;
+  int64_t num_blocks, hkv, row_bytes, layer;
+  int32_t bs, bs_shift;   // bs_shift >= 0 when bs is a power of two
   int64_t nsb, nsh, nst;  // strides of the new K tokens, in bytes
   int64_t vsb, vsh, vst;  // strides of the new V tokens, in bytes
   const int32_t* block_tables;
-  int64_t bt_stride, bt_width;
+  int64_t bt_stride;
+  int32_t bt_width;
   const int32_t* row_ids;
   const int32_t* start_pos;
   const int32_t* new_offsets;
-  int64_t max_new;
+  int32_t max_new;
   int32_t nvec;
   int32_t* err;
 };
 
-// grid: (ceil(max_new * hkv * nvec / blockDim), batch)
-// thread index -> (v fastest, then t, then h) so runs of consecutive threads
-// walk one page row after another.
+constexpr int kAppendTok = 2;  // tokens per thread: both rows' loads are in flight before the stores
+
+// grid: (ceil(max_new / (kAppendTok * blockDim.y)), hkv, batch); block (bx, by)
+// with bx = min(nvec, 256): threadIdx.x walks the 16-byte vectors of a row,
+// threadIdx.y the tokens, so a warp moves whole consecutive rows and no index
+// needs a division (block_size is a shift when it is a power of two).
 template <int VEC>
 __global__ void __launch_bounds__(256) paged_append_kernel(const AppendKernelArgs a) {
   pdl_trigger();  // a dependent launch (the decode plan) may start; it waits for this grid
   using V = typename VecT<VEC>::type;
-  const int64_t b = blockIdx.y;
-  const uint32_t idx = blockIdx.x * blockDim.x + threadIdx.x;
-  const uint32_t nvec = (uint32_t)a.nvec;
-  const uint32_t v = idx % nvec;
-  const uint32_t rest = idx / nvec;
-  const int64_t t = rest % (uint32_t)a.max_new;
-  const int64_t h = rest / (uint32_t)a.max_new;
-  if (h >= a.hkv) return;
-
-  int64_t o_b = 0, n_b = a.max_new;
+  const int b = blockIdx.z;
+  const int h = blockIdx.y;
+  int o_b = 0, n_b = a.max_new;
   if (a.new_offsets) {
     o_b = a.new_offsets[b];
-    n_b = (int64_t)a.new_offsets[b + 1] - o_b;
+    n_b = a.new_offsets[b + 1] - o_b;
   }
-  if (t >= n_b) return;
-
-  const int64_t pos = (int64_t)a.start_pos[b] + t;
-  const int64_t lb = pos / a.bs;
-  const int64_t off = pos - lb * a.bs;
-  if (pos < 0 || lb >= a.bt_width) {
-    raise_dev(a.err, BL_DEVERR_TABLE);
-    return;
-  }
+  const int t0 = blockIdx.x * (kAppendTok * blockDim.y) + threadIdx.y;
+  if (t0 >= n_b) return;
   const int64_t row = a.row_ids ? (int64_t)a.row_ids[b] : b;
-  const int64_t phys = a.block_tables[row * a.bt_stride + lb];
-  if (phys < 0 || phys >= a.num_blocks) {
-    raise_dev(a.err, BL_DEVERR_BLOCK_ID);
-    return;
+  const int32_t start = a.start_pos[b];
+  const char* ksrc = a.k_new + (int64_t)b * a.nsb + (int64_t)h * a.nsh;
+  const char* vsrc = a.v_new + (int64_t)b * a.vsb + (int64_t)h * a.vsh;
+  int64_t src_t[kAppendTok], dst[kAppendTok];
+  bool ok[kAppendTok];
+#pragma unroll
+  for (int i = 0; i < kAppendTok; ++i) {
+    const int t = t0 + i * blockDim.y;
+    ok[i] = t < n_b;
+    src_t[i] = (int64_t)(o_b + t);
+    dst[i] = 0;
+    if (!ok[i]) continue;
+    const int32_t pos = start + t;
+    const int32_t lb = a.bs_shift >= 0 ? (pos >> a.bs_shift) : pos / a.bs;
+    if (pos < 0 || lb >= a.bt_width) {
+      raise_dev(a.err, BL_DEVERR_TABLE);
+      ok[i] = false;
+      continue;
+    }
+    const int64_t phys = a.block_tables[row * a.bt_stride + lb];
+    if (phys < 0 || phys >= a.num_blocks) {
+      raise_dev(a.err, BL_DEVERR_BLOCK_ID);
+      ok[i] = false;
+      continue;
+    }
+    dst[i] = (((a.layer * a.num_blocks + phys) * a.hkv + h) * a.bs + (pos - lb * a.bs)) * a.row_bytes;
   }
-  const int64_t src = b * a.nsb + (o_b + t) * a.nst + h * a.nsh + (int64_t)v * VEC;
-  const int64_t vsrc = b * a.vsb + (o_b + t) * a.vst + h * a.vsh + (int64_t)v * VEC;
-  const int64_t dst = (((a.layer * a.num_blocks + phys) * a.hkv + h) * a.bs + off) * a.row_bytes + (int64_t)v * VEC;
-  const V kv = *reinterpret_cast<const V*>(a.k_new + src);
-  const V vv = *reinterpret_cast<const V*>(a.v_new + vsrc);
-  *reinterpret_cast<V*>(a.k_pool + dst) = kv;
-  *reinterpret_cast<V*>(a.v_pool + dst) = vv;
+  for (int v = threadIdx.x; v < a.nvec; v += blockDim.x) {
+    V kv[kAppendTok], vv[kAppendTok];
+#pragma unroll
+    for (int i = 0; i < kAppendTok; ++i) {
+      if (ok[i]) {
+        kv[i] = *reinterpret_cast<const V*>(ksrc + src_t[i] * a.nst + (int64_t)v * VEC);
+        vv[i] = *reinterpret_cast<const V*>(vsrc + src_t[i] * a.vst + (int64_t)v * VEC);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kAppendTok; ++i) {
+      if (ok[i]) {
+        *reinterpret_cast<V*>(a.k_pool + dst[i] + (int64_t)v * VEC) = kv[i];
+        *reinterpret_cast<V*>(a.v_pool + dst[i] + (int64_t)v * VEC) = vv[i];
+      }
+    }
+  }
 }
 
 struct GatherKernelArgs {
@@ -176,6 +199,9 @@ extern "C" int bl_paged_append(const bl_append_args* args, void* stream) {
                             (uint64_t)(a.v_stride_h * es), (uint64_t)(a.v_stride_t * es)});
   BL_CHECK_ARG(vec > 0, "bl_paged_append: tensors must be at least 2-byte aligned");
 
+  BL_CHECK_ARG(a.max_new_tokens <= INT32_MAX, "bl_paged_append: too many new tokens");
+  BL_CHECK_ARG(a.kv.num_kv_heads <= 65535, "bl_paged_append: too many KV heads");
+
   AppendKernelArgs k;
   k.k_pool = (char*)a.kv.k_pool;
   k.v_pool = (char*)a.kv.v_pool;
@@ -183,9 +209,12 @@ extern "C" int bl_paged_append(const bl_append_args* args, void* stream) {
   k.v_new = (const char*)a.v_new;
   k.num_blocks = a.kv.num_blocks;
   k.hkv = a.kv.num_kv_heads;
-  k.bs = a.kv.block_size;
   k.row_bytes = row_bytes;
   k.layer = a.kv.layer;
+  k.bs = (int32_t)a.kv.block_size;
+  k.bs_shift = -1;
+  for (int sh = 0; sh < 31; ++sh)
+    if ((int64_t)1 << sh == a.kv.block_size) k.bs_shift = sh;
   k.nsb = a.new_stride_b * es;
   k.nsh = a.new_stride_h * es;
   k.nst = a.new_stride_t * es;
@@ -194,25 +223,27 @@ extern "C" int bl_paged_append(const bl_append_args* args, void* stream) {
   k.vst = a.v_stride_t * es;
   k.block_tables = a.kv.block_tables;
   k.bt_stride = a.kv.bt_stride;
-  k.bt_width = a.kv.bt_width;
+  k.bt_width = (int32_t)std::min<int64_t>(a.kv.bt_width, INT32_MAX);
   k.row_ids = a.kv.row_ids;
   k.start_pos = a.start_pos;
   k.new_offsets = a.new_offsets;
-  k.max_new = a.max_new_tokens;
+  k.max_new = (int32_t)a.max_new_tokens;
   k.nvec = (int32_t)(row_bytes / vec);
   k.err = a.err;
 
-  const int64_t per_row = a.max_new_tokens * k.hkv * k.nvec;
-  const int threads = 256;
-  const int64_t gx = (per_row + threads - 1) / threads;
-  BL_CHECK_ARG(gx * threads <= (int64_t)UINT32_MAX, "bl_paged_append: too many tokens per row");
-  dim3 grid((unsigned)gx, (unsigned)a.batch);
+  const int bx = std::min(k.nvec, 256);
+  int by = 256 / bx;  // fewer token rows per block when a row brings few tokens (decode)
+  const int64_t tok_rows = (a.max_new_tokens + kAppendTok - 1) / kAppendTok;
+  while (by > 1 && by / 2 >= tok_rows) by /= 2;
+  const int64_t gx = (a.max_new_tokens + kAppendTok * by - 1) / (kAppendTok * by);
+  dim3 block((unsigned)bx, (unsigned)by);
+  dim3 grid((unsigned)gx, (unsigned)a.kv.num_kv_heads, (unsigned)a.batch);
   cudaStream_t s = (cudaStream_t)stream;
   switch (vec) {
-    case 16: paged_append_kernel<16><<<grid, threads, 0, s>>>(k); break;
-    case 8: paged_append_kernel<8><<<grid, threads, 0, s>>>(k); break;
-    case 4: paged_append_kernel<4><<<grid, threads, 0, s>>>(k); break;
-    default: paged_append_kernel<2><<<grid, threads, 0, s>>>(k); break;
+    case 16: paged_append_kernel<16><<<grid, block, 0, s>>>(k); break;
+    case 8: paged_append_kernel<8><<<grid, block, 0, s>>>(k); break;
+    case 4: paged_append_kernel<4><<<grid, block, 0, s>>>(k); break;
+    default: paged_append_kernel<2><<<grid, block, 0, s>>>(k); break;
   }
   BL_CHECK_LAUNCH("bl_paged_append");
   return BL_OK;

@@ -64,13 +64,8 @@ def _int32_on(t: torch.Tensor, device: torch.device, name: str) -> torch.Tensor:
     return t
 
 
-def _paged_layer(
-    key_cache: torch.Tensor,
-    value_cache: torch.Tensor,
-    layer: int,
-    block_tables: torch.Tensor,
-    row_ids: torch.Tensor | None,
-) -> nat.PagedLayer:
+def _paged_layer_checks(key_cache, value_cache, layer, block_tables, row_ids) -> None:
+    """The pool / table checks one at a time, raising the first that fails."""
     _require_cuda(key_cache, "key_cache")
     _check(key_cache.ndim == 5, "K/V pool must have shape [L, P, H, S, D]")
     _check(key_cache.shape == value_cache.shape, "K/V pools must have identical shape")
@@ -78,25 +73,59 @@ def _paged_layer(
     _check(key_cache.device == value_cache.device, "K/V device must match")
     _check(key_cache.is_contiguous() and value_cache.is_contiguous(), "K/V pools must be contiguous")
     _check(key_cache.dtype in DTYPE_CODE, f"unsupported dtype {key_cache.dtype}")
-    num_layers = key_cache.shape[0]
-    if not 0 <= layer < num_layers:
+    if not 0 <= layer < key_cache.shape[0]:
         raise IndexError(f"Invalid layer index: {layer}")
     _int32_on(block_tables, key_cache.device, "block_tables")
     _check(block_tables.ndim == 2 and block_tables.stride(1) == 1, "block_tables must be [rows, width] with unit inner stride")
     _check(block_tables.shape[1] > 0, "block_tables must have at least one column")
     if row_ids is not None:
         _int32_on(row_ids, key_cache.device, "row_ids")
-    pl = nat.PagedLayer()
-    pl.k_pool = key_cache.data_ptr()
-    pl.v_pool = value_cache.data_ptr()
-    pl.num_layers, pl.num_blocks, pl.num_kv_heads, pl.block_size, pl.head_dim = key_cache.shape
-    pl.dtype = DTYPE_CODE[key_cache.dtype]
-    pl.layer = layer
-    pl.block_tables = block_tables.data_ptr()
-    pl.bt_stride = block_tables.stride(0)
-    pl.bt_width = block_tables.shape[1]
-    pl.row_ids = _ptr(row_ids)
-    return pl
+
+
+def _paged_layer(
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    layer: int,
+    block_tables: torch.Tensor,
+    row_ids: torch.Tensor | None,
+) -> nat.PagedLayer:
+    ks = key_cache.shape
+    dev = key_cache.device
+    dt = key_cache.dtype
+    # every check in one expression (the common, valid case); on a failure
+    # the step-by-step checks raise the specific error
+    if not (len(ks) == 5 and value_cache.shape == ks and value_cache.dtype is dt and dt in DTYPE_CODE
+            and value_cache.device == dev and key_cache.is_contiguous() and value_cache.is_contiguous()
+            and 0 <= layer < ks[0] and block_tables.dtype is torch.int32 and block_tables.device == dev
+            and block_tables.ndim == 2 and block_tables.stride(1) == 1 and block_tables.shape[1] > 0
+            and (row_ids is None or (row_ids.dtype is torch.int32 and row_ids.device == dev))
+            and key_cache.is_cuda):
+        _paged_layer_checks(key_cache, value_cache, layer, block_tables, row_ids)
+    return nat.PagedLayer(key_cache.data_ptr(), value_cache.data_ptr(), ks[0], ks[1], ks[2], ks[3], ks[4],
+                          DTYPE_CODE[dt], layer, block_tables.data_ptr(), block_tables.stride(0),
+                          block_tables.shape[1], None if row_ids is None else row_ids.data_ptr())
+
+
+def _append_checks(key_cache, key, value, start_pos, new_offsets, max_new_tokens) -> None:
+    """paged_append's input checks one at a time, raising the first that fails."""
+    _check(key.ndim == 4 and value.ndim == 4, "K/V must have shape [B, H, T, D]")
+    _check(key.shape == value.shape, "K/V must have identical shape")
+    _check(key.shape[1] == key_cache.shape[2], "KV-head count cannot change")
+    _check(key.shape[2] > 0, "K/V sequence length must be greater than zero")
+    _check(key.shape[3] == key_cache.shape[4], "Head dimension cannot change")
+    _check(key.dtype == key_cache.dtype, "K/V dtype cannot change")
+    _check(key.device == key_cache.device, "K/V device cannot change")
+    _check(key.dtype == value.dtype, "K/V dtype must match")
+    _check(value.device == key_cache.device, "K/V device cannot change")
+    _check(key.stride(3) == 1 and value.stride(3) == 1, "K/V head_dim must be contiguous")
+    _int32_on(start_pos, key.device, "start_pos")
+    batch = start_pos.shape[0]
+    if new_offsets is None:
+        _check(key.shape[0] == batch, "batch size must match number of caches")
+    else:
+        _int32_on(new_offsets, key.device, "new_offsets")
+        _check(key.shape[0] == 1 and new_offsets.shape[0] == batch + 1, "packed K/V need [1, H, T, D] and [B+1] offsets")
+        _check(max_new_tokens is not None and max_new_tokens > 0, "packed append needs max_new_tokens")
 
 
 def paged_append(
@@ -121,41 +150,25 @@ def paged_append(
     Mirrors PagedLayerKV.append_only, src/barellm/engine/paged_kv_cache.py:151-193.
     """
     pl = _paged_layer(key_cache, value_cache, layer, block_tables, row_ids)
-    _check(key.ndim == 4 and value.ndim == 4, "K/V must have shape [B, H, T, D]")
-    _check(key.shape == value.shape, "K/V must have identical shape")
-    _check(key.shape[1] == key_cache.shape[2], "KV-head count cannot change")
-    _check(key.shape[2] > 0, "K/V sequence length must be greater than zero")
-    _check(key.shape[3] == key_cache.shape[4], "Head dimension cannot change")
-    _check(key.dtype == key_cache.dtype, "K/V dtype cannot change")
-    _check(key.device == key_cache.device, "K/V device cannot change")
-    _check(key.dtype == value.dtype, "K/V dtype must match")
-    _check(key.stride(3) == 1 and value.stride(3) == 1, "K/V head_dim must be contiguous")
-    _int32_on(start_pos, key.device, "start_pos")
+    ks = key.shape
+    dev = key_cache.device
     batch = start_pos.shape[0]
-    if new_offsets is None:
-        _check(key.shape[0] == batch, "batch size must match number of caches")
-        max_new = key.shape[2]
-    else:
-        _int32_on(new_offsets, key.device, "new_offsets")
-        _check(key.shape[0] == 1 and new_offsets.shape[0] == batch + 1, "packed K/V need [1, H, T, D] and [B+1] offsets")
-        _check(max_new_tokens is not None and max_new_tokens > 0, "packed append needs max_new_tokens")
-        max_new = int(max_new_tokens)
-    a = nat.AppendArgs()
-    a.kv = pl
-    a.k_new = key.data_ptr()
-    a.v_new = value.data_ptr()
+    packed = new_offsets is not None
+    if not (len(ks) == 4 and value.shape == ks and ks[1] == key_cache.shape[2] and ks[2] > 0
+            and ks[3] == key_cache.shape[4] and key.dtype is key_cache.dtype and value.dtype is key.dtype
+            and key.device == dev and value.device == dev and key.stride(3) == 1 and value.stride(3) == 1
+            and start_pos.dtype is torch.int32 and start_pos.device == dev
+            and (ks[0] == batch if not packed else
+                 (new_offsets.dtype is torch.int32 and new_offsets.device == dev and ks[0] == 1
+                  and new_offsets.shape[0] == batch + 1 and max_new_tokens is not None and max_new_tokens > 0))):
+        _append_checks(key_cache, key, value, start_pos, new_offsets, max_new_tokens)
+    ksd = key.stride()
+    vsd = value.stride()
     # packed rows are addressed by new_offsets alone
-    a.new_stride_b = key.stride(0) if new_offsets is None else 0
-    a.new_stride_h = key.stride(1)
-    a.new_stride_t = key.stride(2)
-    a.v_stride_b = value.stride(0) if new_offsets is None else 0
-    a.v_stride_h = value.stride(1)
-    a.v_stride_t = value.stride(2)
-    a.start_pos = start_pos.data_ptr()
-    a.new_offsets = _ptr(new_offsets)
-    a.batch = batch
-    a.max_new_tokens = max_new
-    a.err = _ptr(err)
+    a = nat.AppendArgs(pl, key.data_ptr(), value.data_ptr(), 0 if packed else ksd[0], ksd[1], ksd[2],
+                       0 if packed else vsd[0], vsd[1], vsd[2], start_pos.data_ptr(),
+                       new_offsets.data_ptr() if packed else None, batch,
+                       int(max_new_tokens) if packed else ks[2], None if err is None else err.data_ptr())
     _raise_rc(nat.load().bl_paged_append(a, _stream(key.device)))
 
 
@@ -222,7 +235,7 @@ def qk_norm_rope_append(
         _check(max_new_tokens is not None and max_new_tokens > 0, "packed append needs max_new_tokens")
         max_new = int(max_new_tokens)
     if q_out is None:
-        q_out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+        q_out = torch.empty_like(q)  # q's memory layout when q is dense, else contiguous
     _check(q_out.shape == q.shape and q_out.stride(3) == 1 and q_out.dtype == q.dtype, "q_out must match q")
     a = nat.QkPrepArgs()
     a.kv = pl
@@ -327,6 +340,27 @@ def plan_serial(device: torch.device) -> int:
     return _PLAN_SERIAL.get(_dev_index(device), 0)
 
 
+def _decode_checks(q, key_cache, seq_lens, out) -> None:
+    """The decode input checks one at a time, raising the first that fails."""
+    _require_cuda(q, "q")
+    if q.ndim == 4:
+        _check(q.shape[2] == 1, "decode takes one query token per request")
+        q3 = q[:, :, 0, :]
+    else:
+        q3 = q
+    _check(q3.ndim == 3, "q must be [B, Hq, D] or [B, Hq, 1, D]")
+    _check(q3.dtype == key_cache.dtype and q3.device == key_cache.device, "q must match the K/V pool dtype and device")
+    _check(q3.shape[2] == key_cache.shape[4], "Head dimension cannot change")
+    _check(q3.stride(2) == 1, "q head_dim must be contiguous")
+    _int32_on(seq_lens, q3.device, "seq_lens")
+    batch, hq, d = q3.shape
+    _check(seq_lens.shape[0] == batch, "batch size must match number of caches")
+    _check(hq % key_cache.shape[2] == 0, "num_heads must divide evenly by num_kv_heads")
+    if out is not None:
+        out3 = out[:, :, 0, :] if out.ndim == 4 else out
+        _check(out3.shape == (batch, hq, d) and out3.stride(2) == 1, "decode output must be [B, Hq, D], D contiguous")
+
+
 def _decode_args(
     q: torch.Tensor,
     key_cache: torch.Tensor,
@@ -343,42 +377,35 @@ def _decode_args(
     err: torch.Tensor | None,
 ) -> tuple[nat.DecodeArgs, torch.Tensor, torch.Tensor]:
     pl = _paged_layer(key_cache, value_cache, layer, block_tables, row_ids)
-    _require_cuda(q, "q")
-    if q.ndim == 4:
-        _check(q.shape[2] == 1, "decode takes one query token per request")
-        q3 = q[:, :, 0, :]
+    qs = q.shape
+    qst = q.stride()
+    nd = len(qs)
+    # [B, Hq, 1, D] and [B, Hq, D] are read through their B / Hq strides
+    if nd == 4:
+        batch, hq, t1, d = qs
+        qd = qst[3]
     else:
-        q3 = q
-    _check(q3.ndim == 3, "q must be [B, Hq, D] or [B, Hq, 1, D]")
-    _check(q3.dtype == key_cache.dtype and q3.device == key_cache.device, "q must match the K/V pool dtype and device")
-    _check(q3.shape[2] == key_cache.shape[4], "Head dimension cannot change")
-    _check(q3.stride(2) == 1, "q head_dim must be contiguous")
-    _int32_on(seq_lens, q3.device, "seq_lens")
-    batch, hq, d = q3.shape
-    _check(seq_lens.shape[0] == batch, "batch size must match number of caches")
-    _check(hq % key_cache.shape[2] == 0, "num_heads must divide evenly by num_kv_heads")
+        batch, hq, d = qs if nd == 3 else (0, 0, 0)
+        t1, qd = 1, qst[2] if nd == 3 else 0
+    dev = key_cache.device
+    if out is not None:
+        os_, ost = out.shape, out.stride()
+        out_ok = (os_ == (batch, hq, d) and ost[2] == 1) or (os_ == (batch, hq, 1, d) and ost[3] == 1)
+    else:
+        out_ok = True
+    if not (nd in (3, 4) and t1 == 1 and q.dtype is key_cache.dtype and q.device == dev and d == key_cache.shape[4]
+            and qd == 1 and seq_lens.dtype is torch.int32 and seq_lens.device == dev
+            and seq_lens.shape[0] == batch and hq % key_cache.shape[2] == 0 and out_ok and q.is_cuda):
+        _decode_checks(q, key_cache, seq_lens, out)
     if out is None:
-        out = torch.empty((batch, hq, d), dtype=q3.dtype, device=q3.device)
-    out3 = out[:, :, 0, :] if out.ndim == 4 else out
-    _check(out3.shape == (batch, hq, d) and out3.stride(2) == 1, "decode output must be [B, Hq, D], D contiguous")
-    nbytes = decode_workspace_bytes(batch, hq, d, key_cache.shape[3], max_seq_len)
+        out = torch.empty((batch, hq, d), dtype=q.dtype, device=q.device)
+    ost = out.stride()
     if ws is None:
-        ws = workspace(q3.device, nbytes)
-    a = nat.DecodeArgs()
-    a.kv = pl
-    a.q = q3.data_ptr()
-    a.q_stride_b, a.q_stride_h = q3.stride(0), q3.stride(1)
-    a.out = out3.data_ptr()
-    a.out_stride_b, a.out_stride_h = out3.stride(0), out3.stride(1)
-    a.seq_lens = seq_lens.data_ptr()
-    a.batch = batch
-    a.num_q_heads = hq
-    a.scale = 1.0 / math.sqrt(d) if scale is None else float(scale)
-    a.workspace = ws.data_ptr()
-    a.workspace_bytes = ws.numel() * ws.element_size()
-    a.max_seq_len = max_seq_len
-    a.plan_ready = 1 if plan_ready else 0
-    a.err = _ptr(err)
+        ws = workspace(q.device, decode_workspace_bytes(batch, hq, d, key_cache.shape[3], max_seq_len))
+    a = nat.DecodeArgs(pl, q.data_ptr(), qst[0], qst[1], out.data_ptr(), ost[0], ost[1], seq_lens.data_ptr(), batch,
+                       hq, 1.0 / math.sqrt(d) if scale is None else float(scale), ws.data_ptr(),
+                       ws.numel() * ws.element_size(), max_seq_len, 1 if plan_ready else 0,
+                       None if err is None else err.data_ptr())
     return a, out, ws
 
 
@@ -444,8 +471,14 @@ def paged_decode(
     a, out, used_ws = _decode_args(q, key_cache, value_cache, layer, block_tables, seq_lens, max_seq_len, scale,
                                    out, row_ids, ws, plan_ready, err)
     lib = nat.load()
-    fn = {"all": lib.bl_paged_decode, "attention": lib.bl_paged_decode_attention,
-          "reduce": lib.bl_paged_decode_reduce}[stage]
+    if stage == "all":
+        fn = lib.bl_paged_decode
+    elif stage == "attention":
+        fn = lib.bl_paged_decode_attention
+    elif stage == "reduce":
+        fn = lib.bl_paged_decode_reduce
+    else:
+        raise KeyError(stage)
     _raise_rc(fn(a, _stream(key_cache.device)))
     if not plan_ready and stage == "all":
         idx = _dev_index(key_cache.device)

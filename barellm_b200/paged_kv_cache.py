@@ -176,6 +176,8 @@ class PagedKVCache:
         self.request_pages: dict[str, _RequestPages] = {}
         self.arena = BlockTableArena(self.device, rows=max_requests, width=64, num_layers=num_layers)
         self._err = None
+        self._generation = 0  # bumped whenever a request gains or loses its arena row
+        self._rows_cache: dict[tuple, tuple[int, np.ndarray]] = {}
 
     # -- error word shared by this pool's kernels -------------------------
     @property
@@ -200,6 +202,7 @@ class PagedKVCache:
         if pages is None:
             pages = _RequestPages(list(blocks), self.arena.alloc_row(), self.arena)
             self.request_pages[request_id] = pages
+            self._generation += 1
         else:
             pages.blocks = list(blocks)
         self.arena.set_row(pages.row, [b.block_id for b in blocks])
@@ -221,6 +224,25 @@ class PagedKVCache:
         pages = self.request_pages.pop(request_id, None)
         if pages is not None:
             self.arena.free_row(pages.row)
+            self._generation += 1
+
+    def rows_for(self, request_ids: tuple) -> np.ndarray:
+        """Arena rows of ``request_ids`` (read-only int64 array).  A decode
+        batch asks for the same requests step after step, so the answer is
+        kept until a request is registered or removed."""
+        hit = self._rows_cache.get(request_ids)
+        if hit is not None and hit[0] == self._generation:
+            return hit[1]
+        pages = self.request_pages
+        try:
+            rows = np.fromiter((pages[r].row for r in request_ids), dtype=np.int64, count=len(request_ids))
+        except KeyError as exc:
+            raise KeyError(f"Unknown request: {exc.args[0]}") from exc
+        rows.flags.writeable = False
+        if len(self._rows_cache) >= 16:
+            self._rows_cache.clear()
+        self._rows_cache[request_ids] = (self._generation, rows)
+        return rows
 
     def get_cache(self, request_id: str) -> "PagedKVCacheView":
         if request_id not in self.request_pages:

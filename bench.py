@@ -53,6 +53,17 @@ WORKLOADS = {
     # paged prefix of U{0..8192} tokens plus a new chunk of U{512..2048}
     "prefill_qwen8b": dict(kind="prefill", hq=32, hkv=8, d=128, bs=16, batch=32, prefix_lo=0, prefix_hi=8192,
                            chunk_lo=512, chunk_hi=2048, pool_blocks=65536, shard_batch=True),
+    # K/V copies on their own (HBM-bound): the chunk append of the prefill
+    # workload (packed ragged chunks into fresh pages after each prefix), the
+    # same chunks through the fused QK-RMSNorm + RoPE + append kernel, and the
+    # dense zero-padded read of the decode workload's pages
+    "append_qwen8b_chunks": dict(kind="copy", op="append", hq=32, hkv=8, d=128, bs=16, batch=32, prefix_lo=0,
+                                 prefix_hi=8192, chunk_lo=512, chunk_hi=2048, pool_blocks=65536, shard_batch=True),
+    "qkprep_qwen8b_chunks": dict(kind="copy", op="qkprep", hq=32, hkv=8, d=128, bs=16, batch=32, prefix_lo=0,
+                                 prefix_hi=8192, chunk_lo=512, chunk_hi=2048, pool_blocks=65536, shard_batch=True),
+    "gather_qwen06b_b64": dict(kind="copy", op="gather", hq=16, hkv=8, d=128, bs=16, batch=64, len_lo=128,
+                               len_hi=4096, log_uniform=False, pool_blocks=65536, shard_batch=False,
+                               scale=1 / math.sqrt(128)),
     # end to end: Qwen3-0.6B architecture, random bf16 weights, 128 requests of
     # random token ids (prompts U{64..2048}) placed across the GPUs, greedy
     # decoding of 256 new tokens through the paged engine
@@ -295,8 +306,9 @@ def time_steps(fn, steps: int, device) -> float:
     return s.elapsed_time(e)
 
 
-def traffic_from_profile(workload: str) -> tuple[float | None, str | None]:
-    p = ROOT / "profiles" / f"decode_tc_kernel.{workload}.json"
+def traffic_from_profile(kernel: str, workload: str) -> tuple[float | None, str | None]:
+    """DRAM bytes per launch of ``kernel`` from its committed ncu summary."""
+    p = ROOT / "profiles" / f"{kernel}.{workload}.json"
     if p.exists():
         d = json.loads(p.read_text())
         return d.get("dram_bytes_per_launch"), d.get("note")
@@ -475,7 +487,7 @@ def run_ours(args, wl_name: str) -> None:
     hbm_peak, peak_src = load_peaks()
     att_bytes = work.decode_bytes()
     achieved = att_bytes / (att_ms / 1e3) / 1e9
-    traffic, traffic_note = traffic_from_profile(wl_name)
+    traffic, traffic_note = traffic_from_profile("decode_tc_kernel", wl_name)
 
     # output sanity vs the oracle on a few rows (not timed)
     del graph
@@ -879,6 +891,379 @@ def run_reference_prefill(args, wl_name: str) -> None:
 
 
 # ---------------------------------------------------------------------------
+# K/V copies: chunk append, fused QK prep + append, dense gather
+# ---------------------------------------------------------------------------
+def rope_tables(positions: np.ndarray, d: int, theta: float, device) -> tuple[torch.Tensor, torch.Tensor]:
+    """cos / sin ``[1, 1, T, D]`` of the half-split rotary embedding at the
+    given positions (inverse frequencies theta^(-2i/D), the angle table
+    repeated over both halves), rounded to bf16."""
+    inv = 1.0 / (theta ** (torch.arange(0, d, 2, dtype=torch.float32, device=device) / d))
+    ang = torch.from_numpy(positions.astype(np.float32)).to(device)[:, None] * inv[None, :]
+    emb = torch.cat((ang, ang), dim=-1)
+    return emb.cos().to(torch.bfloat16)[None, None], emb.sin().to(torch.bfloat16)[None, None]
+
+
+class CopyWorkload:
+    """One GPU's share of a K/V copy workload, device resident.
+
+    append / qkprep: the chunk tokens of the chunked-prefill workload, packed
+    on the token axis in the model's layout (``[1, T, H, D]`` memory viewed
+    as ``[1, H, T, D]``), written into fresh pages after each request's
+    prefix (one launch per step; repeated steps rewrite the same slots).
+    gather: the decode workload's cached tokens read into a zero-padded
+    ``[B, Hkv, Tmax, D]`` K/V pair (the reference's read + pad)."""
+
+    def __init__(self, wl: dict, rank: int, world: int, device: torch.device):
+        self.wl = wl
+        self.op = wl["op"]
+        self.device = device
+        hq, hkv, d, bs = wl["hq"], wl["hkv"], wl["d"], wl["bs"]
+        row = d * 2  # bytes of one bf16 row
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        if self.op == "gather":
+            dw = DecodeWorkload(wl, rank, world, device)
+            self.dw = dw
+            self.batch, self.pool_blocks = dw.batch, dw.pool_blocks
+            self.k_cache, self.v_cache, self.bt = dw.k_cache, dw.v_cache, dw.bt
+            self.lens = list(dw.lens)
+            self.seq = torch.tensor(self.lens, dtype=torch.int32, device=device)
+            self.max_len = max(self.lens)
+            shape = (self.batch, hkv, self.max_len, d)
+            self.k_out = torch.empty(shape, dtype=torch.bfloat16, device=device)
+            self.v_out = torch.empty_like(self.k_out)
+            useful = sum(self.lens) * hkv * row
+            pad = (self.batch * self.max_len - sum(self.lens)) * hkv * row
+            # read + write of every cached K and V row, plus the zero rows of the padding
+            self.bytes = 2 * (2 * useful) + 2 * pad
+            self.tokens = sum(self.lens)
+            self.kernel = "paged_gather_kernel"
+        else:
+            prefix_all, chunk_all = prefill_lengths(wl, 4321)
+            mine = place_requests(prefix_all + chunk_all, world)[rank]
+            self.prefix = [int(prefix_all[i]) for i in mine]
+            self.chunk = [int(chunk_all[i]) for i in mine]
+            b = len(mine)
+            self.batch = b
+            self.pool_blocks = wl["pool_blocks"]
+            rs = np.random.RandomState(4321 + rank)
+            free = list(rs.permutation(self.pool_blocks))
+            totals = [p + c for p, c in zip(self.prefix, self.chunk)]
+            tables = [[int(free.pop()) for _ in range(-(-n // bs))] for n in totals]
+            bt = np.full((b, max(len(t) for t in tables)), -1, dtype=np.int32)
+            for i, t in enumerate(tables):
+                bt[i, : len(t)] = t
+            self.bt = torch.from_numpy(bt).to(device)
+            shape = (1, self.pool_blocks, hkv, bs, d)
+            self.k_cache = torch.empty(shape, dtype=torch.bfloat16, device=device)
+            self.v_cache = torch.empty(shape, dtype=torch.bfloat16, device=device)
+            gen = torch.Generator(device=device)
+            gen.manual_seed(4321 + rank)
+            nc = sum(self.chunk)
+            self.tokens = nc
+            self.k_new = torch.randn((1, nc, hkv, d), generator=gen, device=device).to(torch.bfloat16).transpose(1, 2)
+            self.v_new = torch.randn((1, nc, hkv, d), generator=gen, device=device).to(torch.bfloat16).transpose(1, 2)
+            self.offs = torch.tensor(np.concatenate([[0], np.cumsum(self.chunk)]), dtype=torch.int32, device=device)
+            self.starts = torch.tensor(self.prefix, dtype=torch.int32, device=device)
+            self.max_chunk = max(self.chunk)
+            if self.op == "append":
+                # read + write of every new K and V row
+                self.bytes = 2 * 2 * nc * hkv * row
+                self.kernel = "paged_append_kernel"
+            else:
+                self.q = torch.randn((1, nc, hq, d), generator=gen, device=device).to(torch.bfloat16).transpose(1, 2)
+                self.q_out = torch.empty((1, nc, hq, d), dtype=torch.bfloat16, device=device).transpose(1, 2)
+                self.qw = (1 + 0.1 * torch.randn(d, generator=gen, device=device)).to(torch.bfloat16)
+                self.kw = (1 + 0.1 * torch.randn(d, generator=gen, device=device)).to(torch.bfloat16)
+                pos = np.concatenate([np.arange(p, p + c) for p, c in zip(self.prefix, self.chunk)])
+                self.cos, self.sin = rope_tables(pos, d, 1e6, device)
+                # read + write of every q, k and v row, plus one cos and one sin row per token
+                self.bytes = 2 * nc * (hq + 2 * hkv) * row + 2 * nc * row
+                self.kernel = "qk_prep_kernel"
+        torch.cuda.synchronize(device)
+
+    def step(self) -> None:
+        from barellm_b200 import ops
+
+        if self.op == "gather":
+            ops.paged_gather(self.k_cache, self.v_cache, 0, self.bt, self.seq, self.max_len,
+                             out=(self.k_out, self.v_out), err=self.err)
+        elif self.op == "append":
+            ops.paged_append(self.k_cache, self.v_cache, 0, self.bt, self.starts, self.k_new, self.v_new,
+                             new_offsets=self.offs, max_new_tokens=self.max_chunk, err=self.err)
+        else:
+            ops.qk_norm_rope_append(self.q, self.k_new, self.v_new, self.qw, self.kw, self.cos, self.sin, 1e-6,
+                                    self.k_cache, self.v_cache, 0, self.bt, self.starts, new_offsets=self.offs,
+                                    max_new_tokens=self.max_chunk, q_out=self.q_out, err=self.err)
+
+
+def copy_e2e(work: CopyWorkload, steps: int, warmup: int, device) -> dict:
+    """The same copy through the public cache API with host buffers: append /
+    qkprep through PackedBatchKVCache (inputs copied from pinned host memory
+    every step, the error word or the prepared q read back); gather through
+    BatchKVCache.read (the dense K/V copied back to pinned host memory)."""
+    from barellm_b200 import BatchKVCache, BlockPool, KVCacheManager, PackedBatchKVCache, PagedKVCache, ops
+
+    wl = work.wl
+    hkv, d, bs = wl["hkv"], wl["d"], wl["bs"]
+    if work.op == "gather":
+        lens = work.lens
+    else:
+        lens = [p + c for p, c in zip(work.prefix, work.chunk)]
+    need = sum(-(-n // bs) for n in lens)
+    kv = PagedKVCache(1, need + 64, hkv, bs, d, dtype=torch.bfloat16, device=device, max_requests=work.batch)
+    pool = BlockPool(need + 64)
+    pool.free_ids = [int(x) for x in np.random.RandomState(11).permutation(need + 64)]
+    mgr = KVCacheManager(bs, pool, kv)
+
+    class Req:
+        def __init__(self, i, n):
+            self.id, self.seq_len = f"c{i}", n
+
+    reqs = [Req(i, n) for i, n in enumerate(lens)]
+    for r in reqs:
+        assert mgr.allocate_request(r)
+    views = [mgr.get_cache(r) for r in reqs]
+    rows = np.array([kv.request_pages[v.request_id].row for v in views])
+    if work.op == "gather":
+        for i, vw in enumerate(views):
+            n = lens[i]
+            kd, vd = ops.paged_gather(work.k_cache, work.v_cache, 0, work.bt[i : i + 1],
+                                      torch.tensor([n], dtype=torch.int32, device=device), n)
+            vw.layer(0).append_only(kd, vd)
+            del kd, vd
+        shape = (work.batch, hkv, work.max_len, d)
+        k_h = torch.empty(shape, dtype=torch.bfloat16).pin_memory()
+        v_h = torch.empty(shape, dtype=torch.bfloat16).pin_memory()
+
+        def one():
+            k, v = BatchKVCache(views).layer(0).read()
+            k_h.copy_(k, non_blocking=True)
+            v_h.copy_(v, non_blocking=True)
+
+        h2d, d2h = 0, 2 * k_h.numel() * 2
+    else:
+        prefix = np.array(work.prefix)
+        nc = work.tokens
+        k_h = work.k_new.transpose(1, 2).contiguous().cpu().pin_memory()
+        v_h = work.v_new.transpose(1, 2).contiguous().cpu().pin_memory()
+        k_d, v_d = torch.empty_like(k_h, device=device), torch.empty_like(v_h, device=device)
+        err_h = torch.zeros(1, dtype=torch.int32).pin_memory()
+        h2d, d2h = 2 * k_h.numel() * 2, 4
+        if work.op == "qkprep":
+            q_h = work.q.transpose(1, 2).contiguous().cpu().pin_memory()
+            q_d = torch.empty_like(q_h, device=device)
+            qo_h = torch.empty_like(q_h).pin_memory()
+            h2d += q_h.numel() * 2
+            d2h = qo_h.numel() * 2
+
+        def one():
+            kv.arena.lens[rows, 0] = prefix  # the same chunks are appended again every step
+            k_d.copy_(k_h, non_blocking=True)
+            v_d.copy_(v_h, non_blocking=True)
+            layer = PackedBatchKVCache(views, work.chunk).layer(0)
+            if work.op == "append":
+                layer.append_only(k_d.transpose(1, 2), v_d.transpose(1, 2))
+                err_h.copy_(kv.err, non_blocking=True)
+            else:
+                q_d.copy_(q_h, non_blocking=True)
+                _, qo = layer.append_only_prepped(q_d.transpose(1, 2), k_d.transpose(1, 2), v_d.transpose(1, 2),
+                                                  work.qw, work.kw, work.cos, work.sin, 1e-6)
+                qo_h.copy_(qo.transpose(1, 2), non_blocking=True)
+
+    for _ in range(warmup):
+        one()
+    torch.cuda.synchronize(device)
+    ms = time_steps(one, steps, device)
+    kv.check_device_errors()
+    return {"ms": ms, "h2d": h2d, "d2h": d2h}
+
+
+def copy_cpu(wl: dict, work_like: dict, seconds: float, runs_min: int = 1, warmup: int = 1) -> dict:
+    """The reference's CPU copy for a bounded sample (float32 numpy, one
+    thread): append_only of one request's chunk, apply_rope(norm(.)) of its
+    q / k rows plus the append, or read + pad of a few requests."""
+    from oracle import paged_oracle as orc
+
+    op = wl["op"]
+    hq, hkv, d, bs = wl["hq"], wl["hkv"], wl["d"], wl["bs"]
+    row = d * 2
+    rs = np.random.RandomState(3)
+    if op == "gather":
+        lens = work_like["lens"]
+        need = [-(-n // bs) for n in lens]
+        perm = rs.permutation(sum(need))
+        tables, at = [], 0
+        for k in need:
+            tables.append(perm[at : at + k])
+            at += k
+        kc = rs.standard_normal((1, sum(need), hkv, bs, d)).astype(np.float32)
+        vc = rs.standard_normal((1, sum(need), hkv, bs, d)).astype(np.float32)
+        tmax = max(lens)
+        nbytes = 4 * sum(lens) * hkv * row + 2 * (len(lens) * tmax - sum(lens)) * hkv * row
+
+        def run():
+            orc.batch_read_pad(kc, vc, 0, tables, lens)
+
+        sample = f"read + pad of {len(lens)} requests ({sum(lens)} cached tokens)"
+    else:
+        p, c = work_like["prefix"], work_like["chunk"]
+        nb = -(-(p + c) // bs)
+        kc = np.zeros((1, nb, hkv, bs, d), np.float32)
+        vc = np.zeros_like(kc)
+        table = rs.permutation(nb)
+        k = rs.standard_normal((1, hkv, c, d)).astype(np.float32)
+        v = rs.standard_normal((1, hkv, c, d)).astype(np.float32)
+        if op == "append":
+            nbytes = 4 * c * hkv * row
+
+            def run():
+                orc.append_only(kc, vc, 0, table, p, k, v)
+
+            sample = f"append_only of one request's chunk ({c} tokens after a prefix of {p})"
+        else:
+            q = rs.standard_normal((1, hq, c, d)).astype(np.float32)
+            w = (1 + 0.1 * rs.standard_normal(d)).astype(np.float32)
+            pos = np.arange(p, p + c, dtype=np.float64)
+            inv = 1.0 / (1e6 ** (np.arange(0, d, 2) / d))
+            ang = np.concatenate([pos[:, None] * inv[None]] * 2, axis=-1)
+            cos, sin = np.cos(ang).astype(np.float32)[None, None], np.sin(ang).astype(np.float32)[None, None]
+            nbytes = 2 * c * (hq + 2 * hkv) * row + 2 * c * row
+
+            def run():
+                orc.qk_norm_rope(q, w, cos, sin, 1e-6)
+                kr = orc.qk_norm_rope(k, w, cos, sin, 1e-6).astype(np.float32)
+                orc.append_only(kc, vc, 0, table, p, kr, v)
+
+            sample = f"q/k norm + rope and append_only of one request's chunk ({c} tokens after a prefix of {p})"
+    for _ in range(warmup):
+        run()
+    t0 = time.perf_counter()
+    runs = 0
+    while runs < runs_min or time.perf_counter() - t0 < seconds:
+        run()
+        runs += 1
+    el = (time.perf_counter() - t0) / runs
+    return {"value": round(nbytes / el / 1e9, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"{sample}, {runs} runs of {el:.4f} s, float32 numpy restatement of the reference", "per": el}
+
+
+COPY_METRIC = {"append": "paged K/V append GB/s", "qkprep": "fused QK-norm + RoPE + append GB/s",
+               "gather": "paged K/V dense read GB/s"}
+
+
+def copy_sample(wl: dict, work: CopyWorkload | None = None) -> dict:
+    """The request(s) the CPU sample copies: the workload's first request (its
+    first few for gather)."""
+    if wl["op"] == "gather":
+        lens = work.lens if work is not None else [int(x) for x in request_lengths(wl, 1234)]
+        return {"lens": cpu_sample_lens(lens, 8, 20000)}
+    if work is not None:
+        return {"prefix": work.prefix[0], "chunk": work.chunk[0]}
+    prefix, chunk = prefill_lengths(wl, 4321)
+    return {"prefix": int(prefix[0]), "chunk": int(chunk[0])}
+
+
+def run_copy(args, wl_name: str) -> None:
+    rank, world, local = dist_env()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    wl = WORKLOADS[wl_name]
+    work = CopyWorkload(wl, rank, world, device)
+    steps, warmup = args.steps, args.warmup
+    work.step()
+    torch.cuda.synchronize(device)
+    sampler = ClockSampler(local)
+    barrier(world, device)
+    with sampler:
+        for _ in range(warmup):
+            work.step()
+        ms = time_steps(work.step, steps, device)
+    barrier(world, device)
+    if int(work.err.item()):
+        raise RuntimeError(f"device error word {int(work.err.item())}")
+    ms_max = allreduce(ms, "max", world, device)
+    bytes_all = allreduce(float(work.bytes), "sum", world, device)
+    value = bytes_all * steps / (ms_max / 1e3) / 1e9
+    launch_ms = ms / steps  # one launch per step
+    peak, peak_src = load_peaks()
+    achieved = work.bytes / (launch_ms / 1e3) / 1e9
+    traffic, traffic_note = traffic_from_profile(work.kernel, wl_name)
+    e2e = copy_e2e(work, steps, warmup, device)
+    e2e_ms = allreduce(e2e["ms"], "max", world, device)
+    e2e_value = bytes_all * steps / (e2e_ms / 1e3) / 1e9
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = copy_cpu(wl, copy_sample(wl, work), args.cpu_seconds)
+        cpu.pop("per")
+    if rank == 0:
+        if work.op == "gather":
+            cfg = {"lengths": f"uniform {wl['len_lo']}..{wl['len_hi']}", "requests_per_gpu": work.batch,
+                   "output": "[B, Hkv, Tmax, D] K and V, zero padded", "step": "one paged_gather_kernel launch"}
+        else:
+            cfg = {"prefix": f"uniform {wl['prefix_lo']}..{wl['prefix_hi']}",
+                   "chunk": f"uniform {wl['chunk_lo']}..{wl['chunk_hi']}", "requests_total": wl["batch"],
+                   "tokens_per_gpu": work.tokens,
+                   "step": f"one {work.kernel} launch over the packed chunks"}
+        res = {
+            "metric": COPY_METRIC[work.op],
+            "value": round(value, 2),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": steps,
+            "warmup": warmup,
+            "ms_per_step": ms_max / steps,
+            "higher_is_better": True,
+            "scaling": "strong" if wl["shard_batch"] else "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic",
+            "config": dict({"workload": wl_name, "model_shapes": f"{wl['hq']}q/{wl['hkv']}kv heads, head_dim "
+                            f"{wl['d']}, block_size {wl['bs']}", "pool_blocks_per_gpu": work.pool_blocks,
+                            "bytes_per_step_per_gpu": work.bytes, "parallelism": f"dp{world} by request",
+                            "l2": "bytes per step > L2 (126 MB)"}, **cfg),
+            "roofline": {"kernel": work.kernel, "bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
+                         "peak_source": f"{peak_src} hbm_gbs (copy)", "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic, "traffic_note": traffic_note,
+                         "algorithmic_bytes_per_launch": work.bytes, "launch_ms": launch_ms},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": e2e["h2d"],
+                    "d2h_bytes_per_step": e2e["d2h"], "ms_per_step": e2e_ms / steps,
+                    "path": ("BatchKVCache.read, pinned host outputs" if work.op == "gather" else
+                             "PackedBatchKVCache.append_only" + ("_prepped" if work.op == "qkprep" else "") +
+                             ", pinned host inputs")},
+            "gpu_launches": steps,
+            "clocks": sampler.summary(),
+        }
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def run_reference_copy(args, wl_name: str) -> None:
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    wl = WORKLOADS[wl_name]
+    sample = copy_sample(wl)
+    cpu = copy_cpu(wl, sample, 0.0, runs_min=args.steps, warmup=args.warmup)
+    per = cpu.pop("per")
+    res = {"metric": COPY_METRIC[wl["op"]], "value": cpu["value"], "unit": "GB/s", "n_gpus": world,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": per * 1e3, "higher_is_better": True,
+           "scaling": "strong" if wl["shard_batch"] else "weak", "vs_baseline": None, "dtype": "f32",
+           "data": "synthetic", "config": {"workload": wl_name}, "impl": "reference", "cpu_baseline": cpu,
+           "e2e": {"value": cpu["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(res), flush=True)
+
+
+# ---------------------------------------------------------------------------
 # end to end (model + engine)
 # ---------------------------------------------------------------------------
 def run_e2e(args, wl_name: str) -> None:
@@ -976,6 +1361,9 @@ def main() -> None:
                               "(the reference arm covers the decode and prefill kernels)"}))
             return
         run_e2e(args, args.workload)
+        return
+    if kind == "copy":
+        (run_reference_copy if args.impl == "reference" else run_copy)(args, args.workload)
         return
     if args.impl == "reference":
         (run_reference_prefill if prefill else run_reference)(args, args.workload)
