@@ -41,6 +41,7 @@ EXPORTED = (
     "bl_paged_decode_reduce",
     "bl_paged_decode_noalloc",
     "bl_paged_prefill",
+    "bl_rms_norm",
     "bl_last_error",
     "bl_abi_version",
     "bl_decode_path",
@@ -179,6 +180,24 @@ class QkPrepArgs(Structure):
     ]
 
 
+class RmsNormArgs(Structure):
+    _fields_ = [
+        ("x", c_void_p),
+        ("residual", c_void_p),
+        ("x_out", c_void_p),
+        ("out", c_void_p),
+        ("weight", c_void_p),
+        ("rows", c_int64),
+        ("hidden", c_int64),
+        ("x_stride", c_int64),
+        ("residual_stride", c_int64),
+        ("x_out_stride", c_int64),
+        ("out_stride", c_int64),
+        ("eps", c_float),
+        ("dtype", c_int32),
+    ]
+
+
 STRUCTS = {
     "bl_paged_layer": PagedLayer,
     "bl_qk_prep_args": QkPrepArgs,
@@ -186,6 +205,7 @@ STRUCTS = {
     "bl_gather_args": GatherArgs,
     "bl_decode_args": DecodeArgs,
     "bl_prefill_args": PrefillArgs,
+    "bl_rms_norm_args": RmsNormArgs,
 }
 
 _lib: ctypes.CDLL | None = None
@@ -219,6 +239,8 @@ def load() -> ctypes.CDLL:
     lib.bl_paged_decode_noalloc.restype = c_int
     lib.bl_paged_prefill.argtypes = [POINTER(PrefillArgs), c_void_p]
     lib.bl_paged_prefill.restype = c_int
+    lib.bl_rms_norm.argtypes = [POINTER(RmsNormArgs), c_void_p]
+    lib.bl_rms_norm.restype = c_int
     lib.bl_last_error.argtypes = []
     lib.bl_last_error.restype = c_char_p
     lib.bl_abi_version.argtypes = []

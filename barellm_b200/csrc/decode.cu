@@ -42,6 +42,10 @@ namespace bl {
 namespace {
 
 constexpr int kChunkTokens = 512;  // split-K chunk; fixed so results are batch-invariant
+// The plan kernel stamps its header with this value and the batch size; the
+// attention kernel runs a plan only when both match, so a workspace that holds
+// no plan (or another batch's) yields an error word, not stray reads.
+constexpr int32_t kPlanMagic = 0x4e414c50;
 
 // ---------------------------------------------------------------------------
 // workspace layout
@@ -167,6 +171,8 @@ __global__ void __launch_bounds__(kPlanThreads) decode_plan_kernel(const PlanArg
       total = a.max_units;
     }
     a.hdr[0] = total;
+    a.hdr[1] = kPlanMagic;
+    a.hdr[2] = a.batch;
   }
   __syncthreads();
   // pass 2: scatter partial chunks into their size buckets
@@ -205,7 +211,7 @@ struct TCArgs {
   int32_t bt_width;
   const int32_t* row_ids;
   const int32_t* seq_lens;
-  int32_t hq, hkv, g;
+  int32_t batch, hq, hkv, g;
   int64_t num_blocks;
   int64_t layer_row0;  // layer * num_blocks * hkv * bs (pool row of block 0, head 0)
   float scale_log2;
@@ -225,6 +231,16 @@ struct TCShared {
   uint64_t empty[kStages];
   int abort;
 };
+
+// A plan unit (row, chunk) is used only when the row is in the batch and the
+// chunk lies inside the row's current length; the producer and the consumers
+// apply the same test, so they always agree on the pages of an item.
+__device__ __forceinline__ bool unit_in_range(const TCArgs& a, int2 bc, int& len, int& nbt) {
+  if (bc.x < 0 || bc.x >= a.batch || bc.y < 0) return false;
+  len = a.seq_lens[bc.x];
+  nbt = min((len + kBS - 1) / kBS, a.bt_width);
+  return bc.y * a.chunk_blocks < nbt;
+}
 
 template <typename T>
 __global__ void __launch_bounds__(kThreadsTC) decode_tc_kernel(const TCArgs a,
@@ -253,7 +269,12 @@ __global__ void __launch_bounds__(kThreadsTC) decode_tc_kernel(const TCArgs a,
   __syncthreads();
 
   pdl_wait();  // the plan (and the append before it) are complete and visible
-  const int total_items = a.hdr[0] * a.hkv;
+  int units = a.hdr[0];
+  if (a.hdr[1] != kPlanMagic || a.hdr[2] != a.batch || units < 0 || units > a.max_units) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) raise_dev(a.err, BL_DEVERR_WORKSPACE);
+    units = 0;
+  }
+  const int total_items = units * a.hkv;
   const int cb = a.chunk_blocks;
 
   if (warp == kNW) {
@@ -268,8 +289,11 @@ __global__ void __launch_bounds__(kThreadsTC) decode_tc_kernel(const TCArgs a,
       const int u = item / a.hkv;
       const int h = item - u * a.hkv;
       const int2 bc = a.exec[u];
-      const int len = a.seq_lens[bc.x];
-      const int nbt = min((len + kBS - 1) / kBS, a.bt_width);
+      int len, nbt;
+      if (!unit_in_range(a, bc, len, nbt)) {
+        raise_dev(a.err, BL_DEVERR_WORKSPACE);
+        continue;
+      }
       const int lb0 = bc.y * cb;
       const int nb = min(cb, nbt - lb0);
       const int64_t row = a.row_ids ? (int64_t)a.row_ids[bc.x] : (int64_t)bc.x;
@@ -321,9 +345,9 @@ __global__ void __launch_bounds__(kThreadsTC) decode_tc_kernel(const TCArgs a,
     const int u = item / a.hkv;
     const int h = item - u * a.hkv;
     const int2 bc = a.exec[u];
+    int len, nbt;
+    if (!unit_in_range(a, bc, len, nbt)) continue;  // flagged by the producer
     const int b = bc.x;
-    const int len = a.seq_lens[b];
-    const int nbt = min((len + kBS - 1) / kBS, a.bt_width);
     const int lb0 = bc.y * cb;
     const int nb = min(cb, nbt - lb0);
     const int nch = (nbt + cb - 1) / cb;
@@ -470,7 +494,7 @@ __global__ void __launch_bounds__(kThreadsTC) decode_tc_kernel(const TCArgs a,
         *op = from_f32<T>(val);
       } else {
         const int64_t slot_u = (int64_t)a.row_base[b] + bc.y;
-        if (slot_u >= a.max_units) continue;  // plan overflow, flagged by the plan kernel
+        if (slot_u < 0 || slot_u >= a.max_units) continue;  // plan overflow, flagged by the plan kernel
         a.ws_o[(slot_u * a.hq + hq) * kD + d] = val;
         if (d == 0) a.ws_lse[slot_u * a.hq + hq] = (L > 0.f) ? M + __log2f(L) : -INFINITY;
       }
@@ -506,7 +530,7 @@ __global__ void __launch_bounds__(256) decode_reduce_kernel(const ReduceArgs a) 
   const int nch = (nbt + a.chunk_blocks - 1) / a.chunk_blocks;
   if (nch <= 1) return;
   const int64_t base = a.row_base[b];
-  if (base + nch > a.max_units) return;  // plan overflow, flagged by the plan kernel
+  if (base < 0 || base + nch > a.max_units) return;  // plan overflow, flagged by the plan kernel
   float M = -INFINITY;
   for (int c = 0; c < nch; ++c) M = fmaxf(M, a.ws_lse[(base + c) * a.hq + hq]);
   for (int d = threadIdx.x; d < a.d; d += blockDim.x) {
@@ -677,6 +701,7 @@ int launch_tc_attention(const bl_decode_args& a, const WsLayout& w, cudaStream_t
   k.bt_width = (int32_t)std::min<int64_t>(a.kv.bt_width, INT32_MAX);
   k.row_ids = a.kv.row_ids;
   k.seq_lens = a.seq_lens;
+  k.batch = (int32_t)a.batch;
   k.hq = (int32_t)a.num_q_heads;
   k.hkv = (int32_t)a.kv.num_kv_heads;
   k.g = g;

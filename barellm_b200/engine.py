@@ -21,6 +21,7 @@ import torch
 import torch.nn.functional as F
 from torch import nn
 
+from . import ops
 from .backend import CudaPagedAttentionBackend
 from .batched_kv_cache import BatchKVCache, PackedBatchKVCache
 from .block_pool import BlockPool
@@ -44,6 +45,12 @@ class Qwen3Shape:
 QWEN3_06B = Qwen3Shape()
 
 
+def _fused_norm_ok(x: torch.Tensor) -> bool:
+    """bf16 / fp16 activations on a CUDA device take the one-kernel norm; fp32
+    keeps the tensor-op chain (the exact-match reference runs are fp32)."""
+    return x.is_cuda and x.dtype in (torch.bfloat16, torch.float16) and x.stride(-1) == 1
+
+
 class RMSNorm(nn.Module):
     """fp32 mean-square normalisation, weight applied in fp32, cast back (norm.py)."""
 
@@ -53,9 +60,19 @@ class RMSNorm(nn.Module):
         self.eps = eps
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if _fused_norm_ok(x):
+            return ops.rms_norm(x, self.weight, self.eps)
         xf = x.float()
         xf = xf * torch.rsqrt(xf.pow(2).mean(dim=-1, keepdim=True) + self.eps)
         return (xf * self.weight).to(x.dtype)
+
+    def add_forward(self, x: torch.Tensor, residual: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """``(x + residual, norm(x + residual))``: one kernel for 16-bit CUDA
+        activations."""
+        if _fused_norm_ok(x) and residual.stride(-1) == 1:
+            return ops.rms_norm(x, self.weight, self.eps, residual=residual)
+        y = x + residual
+        return y, self(y)
 
 
 def rope_cos_sin(head_dim: int, theta: float, position_ids: torch.Tensor, dtype: torch.dtype):
@@ -84,13 +101,38 @@ class Attention(nn.Module):
         self.k_norm = RMSNorm(s.head_dim, s.rms_norm_eps)
         self.backend = backend
         self.fused_prep = True  # QK-norm + RoPE + append in one kernel when the cache is paged
+        self._qkv: torch.Tensor | None = None  # [q; k; v] weights, the three projections are views into it
+
+    def fuse_projections(self) -> None:
+        """One [q; k; v] weight matrix (one GEMM per forward instead of three);
+        q_proj / k_proj / v_proj keep their parameters as views into it."""
+        w = torch.cat([self.q_proj.weight, self.k_proj.weight, self.v_proj.weight]).detach()
+        nq, nk = self.q_proj.weight.shape[0], self.k_proj.weight.shape[0]
+        self.q_proj.weight = nn.Parameter(w[:nq], requires_grad=False)
+        self.k_proj.weight = nn.Parameter(w[nq : nq + nk], requires_grad=False)
+        self.v_proj.weight = nn.Parameter(w[nq + nk :], requires_grad=False)
+        self._qkv = w
+
+    def _projections(self, x: torch.Tensor):
+        b, t, _ = x.shape
+        s = self.s
+        nq, nk = s.num_heads * s.head_dim, s.num_kv_heads * s.head_dim
+        w = self._qkv
+        if w is not None and w.data_ptr() == self.q_proj.weight.data_ptr() and w.dtype == x.dtype:
+            qkv = F.linear(x, w)
+            q = qkv[..., :nq].view(b, t, s.num_heads, s.head_dim)
+            k = qkv[..., nq : nq + nk].view(b, t, s.num_kv_heads, s.head_dim)
+            v = qkv[..., nq + nk :].view(b, t, s.num_kv_heads, s.head_dim)
+        else:
+            q = self.q_proj(x).view(b, t, s.num_heads, s.head_dim)
+            k = self.k_proj(x).view(b, t, s.num_kv_heads, s.head_dim)
+            v = self.v_proj(x).view(b, t, s.num_kv_heads, s.head_dim)
+        return q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
 
     def forward(self, x, cos, sin, layer_cache) -> torch.Tensor:
         b, t, _ = x.shape
         s = self.s
-        q = self.q_proj(x).view(b, t, s.num_heads, s.head_dim).transpose(1, 2)
-        k = self.k_proj(x).view(b, t, s.num_kv_heads, s.head_dim).transpose(1, 2)
-        v = self.v_proj(x).view(b, t, s.num_kv_heads, s.head_dim).transpose(1, 2)
+        q, k, v = self._projections(x)
         group = s.num_heads // s.num_kv_heads
         prepped = getattr(self.backend, "attend_prepped", None)
         if self.fused_prep and prepped is not None and layer_cache is not None:
@@ -113,11 +155,30 @@ class Block(nn.Module):
         self.gate_proj = nn.Linear(s.hidden_size, s.intermediate_size, bias=False)
         self.up_proj = nn.Linear(s.hidden_size, s.intermediate_size, bias=False)
         self.down_proj = nn.Linear(s.intermediate_size, s.hidden_size, bias=False)
+        self._gate_up: torch.Tensor | None = None  # [gate; up] weights, the two projections are views into it
+
+    def fuse_projections(self) -> None:
+        """One [gate; up] weight matrix (one GEMM instead of two) and the
+        attention's fused [q; k; v]."""
+        w = torch.cat([self.gate_proj.weight, self.up_proj.weight]).detach()
+        n = self.gate_proj.weight.shape[0]
+        self.gate_proj.weight = nn.Parameter(w[:n], requires_grad=False)
+        self.up_proj.weight = nn.Parameter(w[n:], requires_grad=False)
+        self._gate_up = w
+        self.self_attn.fuse_projections()
+
+    def _mlp(self, h: torch.Tensor) -> torch.Tensor:
+        w = self._gate_up
+        if w is not None and w.data_ptr() == self.gate_proj.weight.data_ptr() and w.dtype == h.dtype:
+            gu = F.linear(h, w)
+            n = self.gate_proj.weight.shape[0]
+            return self.down_proj(F.silu(gu[..., :n]) * gu[..., n:])
+        return self.down_proj(F.silu(self.gate_proj(h)) * self.up_proj(h))
 
     def forward(self, x, cos, sin, layer_cache) -> torch.Tensor:
-        x = x + self.self_attn(self.input_layernorm(x), cos, sin, layer_cache)
-        h = self.post_attention_layernorm(x)
-        return x + self.down_proj(F.silu(self.gate_proj(h)) * self.up_proj(h))
+        a = self.self_attn(self.input_layernorm(x), cos, sin, layer_cache)
+        x, h = self.post_attention_layernorm.add_forward(x, a)
+        return x + self._mlp(h)
 
 
 class Qwen3(nn.Module):
@@ -131,6 +192,13 @@ class Qwen3(nn.Module):
         nn.init.normal_(self.embed, mean=0.0, std=0.02)
         self.layers = nn.ModuleList([Block(s, self.backend) for _ in range(s.num_layers)])
         self.norm = RMSNorm(s.hidden_size, s.rms_norm_eps)
+
+    def fuse_projections(self) -> None:
+        """Fused [q; k; v] and [gate; up] weights in every block (same values,
+        fewer GEMM launches); idempotent."""
+        for blk in self.layers:
+            if blk._gate_up is None:
+                blk.fuse_projections()
 
     def set_backend(self, backend) -> None:
         self.backend = backend
@@ -210,6 +278,7 @@ class PagedEngine:
         dev = next(model.parameters()).device
         dtype = next(model.parameters()).dtype
         self.model = model
+        model.fuse_projections()
         self.block_size = block_size
         self.cache = PagedKVCache(s.num_layers, num_blocks, s.num_kv_heads, block_size, s.head_dim, dtype=dtype,
                                   device=dev, max_requests=max_requests)

@@ -592,6 +592,50 @@ def paged_prefill(
     return out
 
 
+def rms_norm(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    eps: float,
+    *,
+    residual: torch.Tensor | None = None,
+    out: torch.Tensor | None = None,
+    x_out: torch.Tensor | None = None,
+) -> torch.Tensor | tuple[torch.Tensor, torch.Tensor]:
+    """RMSNorm over the last axis in one kernel (decoder support around the
+    attention path): ``rmsnorm(x) * weight`` with the reference's roundings
+    (src/barellm/models/norm.py:14-21).  With ``residual`` it first forms
+    ``x + residual`` (rounded to the element type, as a tensor add) and returns
+    ``(x + residual, rmsnorm(x + residual) * weight)``.  Rows may be strided;
+    the last axis must be contiguous."""
+    _require_cuda(x, "x")
+    h = x.shape[-1]
+    _check(weight.shape == (h,) and weight.dtype == x.dtype and weight.device == x.device and weight.stride(0) == 1,
+           "norm weight must be [hidden] of the input's dtype and device")
+    _check(x.dtype in DTYPE_CODE, f"unsupported dtype {x.dtype}")
+    _check(x.stride(-1) == 1, "x must have a contiguous last dimension")
+    x2 = x.reshape(-1, h) if x.dim() != 2 else x
+    _check(x2.stride(-1) == 1, "x rows must be addressable with one stride")
+    rows = x2.shape[0]
+    if out is None:
+        out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    o2 = out.view(-1, h)
+    r2 = None
+    xo2 = None
+    if residual is not None:
+        _check(residual.shape == x.shape and residual.dtype == x.dtype and residual.device == x.device,
+               "residual must match x")
+        r2 = residual.reshape(-1, h)
+        _check(r2.stride(-1) == 1, "residual must have a contiguous last dimension")
+        if x_out is None:
+            x_out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+        xo2 = x_out.view(-1, h)
+    a = nat.RmsNormArgs(x2.data_ptr(), None if r2 is None else r2.data_ptr(), None if xo2 is None else xo2.data_ptr(),
+                        o2.data_ptr(), weight.data_ptr(), rows, h, x2.stride(0), 0 if r2 is None else r2.stride(0),
+                        0 if xo2 is None else xo2.stride(0), o2.stride(0), float(eps), DTYPE_CODE[x.dtype])
+    _raise_rc(nat.load().bl_rms_norm(a, _stream(x.device)))
+    return out if residual is None else (x_out, out)
+
+
 def decode_path(dtype: torch.dtype, head_dim: int, block_size: int, num_q_heads: int, num_kv_heads: int) -> int:
     return int(nat.load().bl_decode_path(DTYPE_CODE[dtype], head_dim, block_size, num_q_heads, num_kv_heads))
 

@@ -291,6 +291,35 @@ typedef struct bl_prefill_args {
 BL_API int bl_paged_prefill(const bl_prefill_args* args, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* Decoder support: residual add + RMSNorm (not part of the paged-KV path)   */
+/*
+ * The norm around each attention call of the decoder that drives the path:
+ *   h = rmsnorm(x) * weight                      (models/norm.py:14-21), or
+ *   x_out = x + residual; h = rmsnorm(x_out) * weight   (models/block.py)
+ * with the reference's roundings: the add rounded to the element type, the
+ * mean square, rsqrt and the two products in fp32, one rounding at the end.
+ * Rows of `hidden` elements; each row pointer advances by its own stride
+ * (elements).  `residual` / `x_out` may both be NULL (plain norm).
+ */
+typedef struct bl_rms_norm_args {
+  const void* x;
+  const void* residual;
+  void* x_out;
+  void* out;
+  const void* weight; /* [hidden] */
+  int64_t rows;
+  int64_t hidden;
+  int64_t x_stride;
+  int64_t residual_stride;
+  int64_t x_out_stride;
+  int64_t out_stride;
+  float eps;
+  int32_t dtype;
+} bl_rms_norm_args;
+
+BL_API int bl_rms_norm(const bl_rms_norm_args* args, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* Misc.                                                                     */
 BL_API const char* bl_last_error(void);
 BL_API int bl_abi_version(void);
