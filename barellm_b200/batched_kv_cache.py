@@ -33,30 +33,49 @@ class StepMeta:
     With ``static_max_seq_len`` the device buffers are allocated once and
     ``refresh`` rewrites them in place (one pinned host-to-device copy), so a
     captured CUDA graph that reads them stays valid from step to step;
-    ``max_seq_len`` is then the fixed bound the graph was captured with."""
+    ``max_seq_len`` is then the fixed bound the graph was captured with.
+
+    ``renew`` reuses the object for the next step of the same batch: the
+    device buffers are kept and the new lengths go in with one copy from a
+    fresh pinned buffer (the pinned allocator does not hand that memory out
+    again before the copy has run)."""
 
     def __init__(self, storage: PagedKVCache, rows: np.ndarray, starts: np.ndarray, new_tokens: int,
                  static_max_seq_len: int | None = None) -> None:
-        b = len(rows)
-        host = torch.empty((3, b), dtype=torch.int32, pin_memory=storage.device.type == "cuda")
-        self._host = host
-        h = host.numpy()
-        h[0] = rows
-        h[1] = starts
-        np.add(starts, new_tokens, out=h[2], casting="unsafe")
+        self._pin = storage.device.type == "cuda"
+        self._rows = rows
+        host = self._fill(starts, new_tokens)
         self._dev = host.to(storage.device, non_blocking=True)
         self.rows, self.starts, self.seq_lens = self._dev.unbind(0)
-        self.seq_lens_host = h[2].astype(np.int64)
         self.static = static_max_seq_len is not None
         self.max_seq_len = int(static_max_seq_len) if self.static else int(self.seq_lens_host.max())
         self.new_tokens = new_tokens
+        self.version = 0  # bumped by renew
         self.plan_ws: torch.Tensor | None = None
         self.plan_heads = 0
         self.plan_token = -1
 
+    def _fill(self, starts: np.ndarray, new_tokens: int) -> torch.Tensor:
+        host = torch.empty((3, len(self._rows)), dtype=torch.int32, pin_memory=self._pin)
+        h = host.numpy()
+        h[0] = self._rows
+        h[1] = starts
+        np.add(starts, new_tokens, out=h[2], casting="unsafe")
+        self._host = host
+        self.seq_lens_host = h[2].astype(np.int64)
+        return host
+
     def matches(self, starts: np.ndarray, new_tokens: int) -> bool:
         h = self._host.numpy()
         return new_tokens == self.new_tokens and np.array_equal(h[1], starts)
+
+    def renew(self, starts: np.ndarray, new_tokens: int) -> None:
+        """The next step's lengths into the same device buffers (same rows)."""
+        self._dev.copy_(self._fill(starts, new_tokens), non_blocking=True)
+        self.max_seq_len = int(self.seq_lens_host.max())
+        self.new_tokens = new_tokens
+        self.version += 1
+        self.plan_ws = None  # the lengths changed: the plan must be rebuilt
 
     def stage(self, starts: np.ndarray, new_tokens: int) -> None:
         """Static mode, for graph replay: write the next step's lengths into the
@@ -82,19 +101,25 @@ class StepMeta:
 class BatchKVCache:
     """``static_max_seq_len``: keep one set of device metadata buffers for the
     life of this view (refreshed in place each step) so the decode step can be
-    captured in a CUDA graph; lengths may not exceed the bound."""
+    captured in a CUDA graph; lengths may not exceed the bound.
+
+    Without it, a batch over the same requests as an earlier batch (the
+    engine builds a new BatchKVCache every decode step) reuses that batch's
+    device metadata buffers, renewed with the new lengths."""
 
     def __init__(self, caches: list[PagedKVCacheView], *, static_max_seq_len: int | None = None) -> None:
         check(len(caches) > 0, "batch cache cannot be empty")
         self.caches = caches
-        self._meta: dict[tuple[bytes, int], StepMeta] = {}
+        self._meta: dict[tuple[bytes, int], tuple[StepMeta, int]] = {}
         self._static: StepMeta | None = None
+        self._rowset = None
         first = getattr(caches[0], "storage", None)
         self.storage: PagedKVCache | None = None
         if (isinstance(first, PagedKVCache) and all(issubclass(t, PagedKVCacheView) for t in set(map(type, caches)))
                 and set(map(_STORAGE, caches)) == {first}):
             self.storage = first
-            self.rows = first.rows_for(tuple(map(_REQUEST_ID, caches)))
+            self._rowset = first.row_set(tuple(map(_REQUEST_ID, caches)))
+            self.rows = self._rowset.rows
             if static_max_seq_len is not None:
                 zeros = np.zeros(len(caches), dtype=np.int64)
                 self._static = StepMeta(first, self.rows, zeros, 0, static_max_seq_len=static_max_seq_len)
@@ -110,10 +135,23 @@ class BatchKVCache:
                 self._static.refresh(starts, new_tokens)
             return self._static
         key = (starts.tobytes(), new_tokens)
-        meta = self._meta.get(key)
-        if meta is None:
+        hit = self._meta.get(key)
+        if hit is not None and hit[0].version == hit[1]:
+            return hit[0]
+        rs = self._rowset
+        shared = rs.meta
+        if shared is None:
+            meta = rs.meta = StepMeta(self.storage, self.rows, starts, new_tokens)
+        elif hit is None and shared.matches(starts, new_tokens):
+            meta = shared
+        elif hit is None:
+            shared.renew(starts, new_tokens)
+            meta = shared
+        else:
+            # this batch's buffers were renewed by another batch over the same
+            # requests since: keep a private copy for the rest of this step
             meta = StepMeta(self.storage, self.rows, starts, new_tokens)
-            self._meta = {key: meta}  # one live step per batch view
+        self._meta = {key: (meta, meta.version)}  # one live step per batch view
         return meta
 
 
@@ -212,8 +250,8 @@ class BatchLayerKV:
         st = self.owner._static
         if st is not None and np.array_equal(st.seq_lens_host, cur):
             return st
-        for meta in self.owner._meta.values():
-            if np.array_equal(meta.seq_lens_host, cur):
+        for meta, version in self.owner._meta.values():
+            if meta.version == version and np.array_equal(meta.seq_lens_host, cur):
                 return meta
         return self.owner.step_meta(cur, 0)
 

@@ -142,6 +142,17 @@ class PagedBatchKVMetadata:
     block_size: int
 
 
+class _RowSet:
+    """Arena rows of one request tuple, and that batch's reusable step metadata."""
+
+    __slots__ = ("generation", "rows", "meta")
+
+    def __init__(self, generation: int, rows: np.ndarray) -> None:
+        self.generation = generation
+        self.rows = rows
+        self.meta = None
+
+
 class PagedKVCache:
     """Paged K/V storage for one GPU (one BlockPool shard)."""
 
@@ -177,7 +188,7 @@ class PagedKVCache:
         self.arena = BlockTableArena(self.device, rows=max_requests, width=64, num_layers=num_layers)
         self._err = None
         self._generation = 0  # bumped whenever a request gains or loses its arena row
-        self._rows_cache: dict[tuple, tuple[int, np.ndarray]] = {}
+        self._rows_cache: dict[tuple, _RowSet] = {}
 
     # -- error word shared by this pool's kernels -------------------------
     @property
@@ -209,6 +220,11 @@ class PagedKVCache:
 
     def check_new_kv(self, key: torch.Tensor, value: torch.Tensor, batch: int = 1) -> None:
         """The reference's append checks (paged_kv_cache.py:156-174)."""
+        ks = key.shape
+        if (len(ks) == 4 and value.shape == ks and ks[0] == batch and ks[1] == self.num_kv_heads and ks[2] > 0
+                and ks[3] == self.head_dim and key.dtype is self.dtype and value.dtype is self.dtype
+                and key.device == self.device and value.device == self.device):
+            return
         check(key.ndim == 4 and value.ndim == 4, "K/V must have shape [B, H, T, D]")
         check(key.shape == value.shape, "K/V must have identical shape")
         check(key.shape[0] == batch, "PagedKVCache currently supports batch size 1")
@@ -226,13 +242,14 @@ class PagedKVCache:
             self.arena.free_row(pages.row)
             self._generation += 1
 
-    def rows_for(self, request_ids: tuple) -> np.ndarray:
-        """Arena rows of ``request_ids`` (read-only int64 array).  A decode
-        batch asks for the same requests step after step, so the answer is
-        kept until a request is registered or removed."""
+    def row_set(self, request_ids: tuple) -> "_RowSet":
+        """Arena rows of ``request_ids`` (a read-only int64 array) plus a slot
+        for the batch's reusable step metadata.  A decode batch asks for the
+        same requests step after step, so the answer is kept until a request
+        is registered or removed."""
         hit = self._rows_cache.get(request_ids)
-        if hit is not None and hit[0] == self._generation:
-            return hit[1]
+        if hit is not None and hit.generation == self._generation:
+            return hit
         pages = self.request_pages
         try:
             rows = np.fromiter((pages[r].row for r in request_ids), dtype=np.int64, count=len(request_ids))
@@ -241,8 +258,11 @@ class PagedKVCache:
         rows.flags.writeable = False
         if len(self._rows_cache) >= 16:
             self._rows_cache.clear()
-        self._rows_cache[request_ids] = (self._generation, rows)
-        return rows
+        rs = self._rows_cache[request_ids] = _RowSet(self._generation, rows)
+        return rs
+
+    def rows_for(self, request_ids: tuple) -> np.ndarray:
+        return self.row_set(request_ids).rows
 
     def get_cache(self, request_id: str) -> "PagedKVCacheView":
         if request_id not in self.request_pages:

@@ -349,3 +349,57 @@ def test_backend_rejects_unknown_cache_types(native_lib):
     x = torch.zeros(1, 2, 1, 128, device=DEV).bfloat16()
     with pytest.raises(TypeError, match="paged"):
         CudaPagedAttentionBackend().attend(x, x, x, Contiguous(), 1)
+
+
+def test_successive_batches_reuse_and_protect_step_metadata(native_lib):
+    """An engine builds a new BatchKVCache over the same requests every decode
+    step: the new batch renews the previous one's device metadata in place.
+    A batch whose metadata another batch has renewed since (interleaved use)
+    falls back to private metadata and stays correct."""
+    lengths = [700, 33, 1030]
+    hq, hkv, d, bs = 16, 8, 128, 16
+    rs = np.random.RandomState(7)
+    need = sum(-(-(n + 3) // bs) for n in lengths)
+    storage = PagedKVCache(2, need + 4, hkv, bs, d, dtype=torch.bfloat16, device=DEV)
+    mgr = KVCacheManager(bs, BlockPool(need + 4), storage)
+
+    class R:
+        def __init__(self, rid, n):
+            self.id, self.seq_len = rid, n
+
+    reqs = [R(f"r{i}", n + 3) for i, n in enumerate(lengths)]
+    for r in reqs:
+        assert mgr.allocate_request(r)
+    caches = [mgr.get_cache(r) for r in reqs]
+    for layer in range(2):
+        for c, n in zip(caches, lengths):
+            t = torch.from_numpy(rs.standard_normal((1, hkv, n, d)).astype(np.float32)).bfloat16().to(DEV)
+            c.layer(layer).append_only(t, t * 0.5)
+    be = CudaPagedAttentionBackend()
+
+    def step(batch, layer):
+        q = torch.randn(3, hq, 1, d, device=DEV).bfloat16()
+        k = torch.randn(3, hkv, 1, d, device=DEV).bfloat16()
+        out = be.attend(q, k, k * 0.5, batch.layer(layer), hq // hkv)
+        seq = [int(x) for x in storage.arena.lens[batch.rows, layer]]
+        kc = storage.key_cache.float().cpu().numpy()
+        vc = storage.value_cache.float().cpu().numpy()
+        tables = [storage.request_pages[c.request_id].block_table.cpu().numpy() for c in caches]
+        ref = orc.decode_attention(q.float().cpu().numpy(), kc, vc, layer, tables, seq)
+        err = np.abs(out.float().cpu().numpy() - ref)
+        assert err.max() <= 2e-2 and err.mean() <= 2e-3
+
+    first = BatchKVCache(caches)
+    step(first, 0)
+    step(first, 1)
+    second = BatchKVCache(caches)  # next step: renews the first batch's buffers
+    step(second, 0)
+    (meta_a, _), = first._meta.values()
+    (meta_b, _), = second._meta.values()
+    assert meta_a is meta_b
+    third = BatchKVCache(caches)  # a third step starts on layer 0 ...
+    step(third, 0)
+    step(second, 1)  # ... before the second finishes layer 1: private metadata
+    (meta_b2, _), = second._meta.values()
+    assert meta_b2 is not meta_b
+    step(third, 1)
