@@ -306,11 +306,17 @@ def time_steps(fn, steps: int, device) -> float:
     return s.elapsed_time(e)
 
 
-def traffic_from_profile(kernel: str, workload: str) -> tuple[float | None, str | None]:
-    """DRAM bytes per launch of ``kernel`` from its committed ncu summary."""
+def traffic_from_profile(kernel: str, workload: str, algorithmic_bytes: float | None = None
+                         ) -> tuple[float | None, str | None]:
+    """DRAM bytes per launch of ``kernel`` from its committed ncu summary.  A
+    summary captured on a smaller case of the workload (the full one is too
+    large to capture) gives traffic / algorithmic bytes, applied to this
+    launch's algorithmic bytes."""
     p = ROOT / "profiles" / f"{kernel}.{workload}.json"
     if p.exists():
         d = json.loads(p.read_text())
+        if d.get("traffic_ratio") is not None and algorithmic_bytes is not None:
+            return round(d["traffic_ratio"] * algorithmic_bytes), d.get("note")
         return d.get("dram_bytes_per_launch"), d.get("note")
     return None, None
 
@@ -487,7 +493,7 @@ def run_ours(args, wl_name: str) -> None:
     hbm_peak, peak_src = load_peaks()
     att_bytes = work.decode_bytes()
     achieved = att_bytes / (att_ms / 1e3) / 1e9
-    traffic, traffic_note = traffic_from_profile("decode_tc_kernel", wl_name)
+    traffic, traffic_note = traffic_from_profile("decode_tc_kernel", wl_name, att_bytes)
 
     # output sanity vs the oracle on a few rows (not timed)
     del graph
@@ -1348,9 +1354,15 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--pool-blocks", type=int, default=0,
                     help="override the KV pool size in blocks (smaller profiling captures)")
+    ap.add_argument("--requests", type=int, default=0,
+                    help="override the number of requests (smaller profiling captures)")
     args = ap.parse_args()
-    if args.pool_blocks > 0 and "pool_blocks" in WORKLOADS[args.workload]:
-        WORKLOADS[args.workload]["pool_blocks"] = args.pool_blocks
+    wl = WORKLOADS[args.workload]
+    if args.pool_blocks > 0 and ("pool_blocks" in wl or "pool_bytes" in wl):
+        wl.pop("pool_bytes", None)
+        wl["pool_blocks"] = args.pool_blocks
+    if args.requests > 0 and "batch" in wl:
+        wl["batch"] = args.requests
     if args.warmup < 3:
         args.warmup = 3
     kind = WORKLOADS[args.workload].get("kind")
