@@ -40,6 +40,10 @@ EXPORTED = (
     "bl_paged_decode_attention",
     "bl_paged_decode_reduce",
     "bl_paged_decode_noalloc",
+    "bl_paged_decode_allgather",
+    "bl_ipc_export",
+    "bl_ipc_import",
+    "bl_ipc_close",
     "bl_paged_prefill",
     "bl_rms_norm",
     "bl_last_error",
@@ -123,6 +127,25 @@ class DecodeArgs(Structure):
     ]
 
 
+BL_MAX_RANKS = 8
+
+
+class HeadGather(Structure):
+    _fields_ = [
+        ("world", c_int32),
+        ("rank", c_int32),
+        ("peer_out", c_void_p * BL_MAX_RANKS),
+        ("peer_signal", c_void_p * BL_MAX_RANKS),
+        ("epoch", c_void_p),
+        ("head_offset", c_int64),
+        ("timeout_ns", c_int64),
+    ]
+
+
+class IpcHandle(Structure):
+    _fields_ = [("bytes", ctypes.c_ubyte * 64), ("offset", ctypes.c_uint64)]
+
+
 class PrefillArgs(Structure):
     _fields_ = [
         ("kv", PagedLayer),
@@ -204,6 +227,8 @@ STRUCTS = {
     "bl_append_args": AppendArgs,
     "bl_gather_args": GatherArgs,
     "bl_decode_args": DecodeArgs,
+    "bl_head_gather": HeadGather,
+    "bl_ipc_handle": IpcHandle,
     "bl_prefill_args": PrefillArgs,
     "bl_rms_norm_args": RmsNormArgs,
 }
@@ -237,6 +262,14 @@ def load() -> ctypes.CDLL:
         fn.restype = c_int
     lib.bl_paged_decode_noalloc.argtypes = [POINTER(DecodeArgs), c_void_p]
     lib.bl_paged_decode_noalloc.restype = c_int
+    lib.bl_paged_decode_allgather.argtypes = [POINTER(DecodeArgs), POINTER(HeadGather), c_void_p]
+    lib.bl_paged_decode_allgather.restype = c_int
+    lib.bl_ipc_export.argtypes = [c_void_p, POINTER(IpcHandle)]
+    lib.bl_ipc_export.restype = c_int
+    lib.bl_ipc_import.argtypes = [POINTER(IpcHandle), POINTER(c_void_p)]
+    lib.bl_ipc_import.restype = c_int
+    lib.bl_ipc_close.argtypes = [c_void_p]
+    lib.bl_ipc_close.restype = c_int
     lib.bl_paged_prefill.argtypes = [POINTER(PrefillArgs), c_void_p]
     lib.bl_paged_prefill.restype = c_int
     lib.bl_rms_norm.argtypes = [POINTER(RmsNormArgs), c_void_p]

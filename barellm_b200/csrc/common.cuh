@@ -113,6 +113,45 @@ __device__ __forceinline__ void raise_dev(int32_t* err, int32_t bit) {
 }
 
 // ----------------------------------------------------------------------------
+// output targets: an attention result is stored to one buffer, or -- for the
+// KV-head-sharded decode -- to every rank's copy of the gathered output
+// (peer buffers mapped into this process), so the all-gather rides on the
+// epilogue's own stores
+// ----------------------------------------------------------------------------
+constexpr int kMaxRanks = BL_MAX_RANKS;
+
+struct OutTargets {
+  void* ptr[kMaxRanks];
+  int32_t n;
+};
+
+inline OutTargets one_target(void* p) {
+  OutTargets t = {};
+  t.ptr[0] = p;
+  t.n = 1;
+  return t;
+}
+
+// The loop is unrolled over the fixed bound so every ptr[] index is static
+// (no local-memory copy of the kernel parameter).
+template <typename T>
+__device__ __forceinline__ void store_targets(const OutTargets& o, int64_t off, T v) {
+#pragma unroll
+  for (int p = 0; p < kMaxRanks; ++p)
+    if (p < o.n) reinterpret_cast<T*>(o.ptr[p])[off] = v;
+}
+
+// Release / acquire at system scope, for flags another GPU reads or writes.
+__device__ __forceinline__ void st_release_sys(int32_t* p, int32_t v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int32_t ld_acquire_sys(const int32_t* p) {
+  int32_t v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// ----------------------------------------------------------------------------
 // PTX wrappers
 // ----------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -448,5 +487,16 @@ bool make_tmap_2d_16bit(CUtensorMap* map, const void* base, uint64_t row_elems, 
 // Cached tensor map over a K or V pool viewed as `rows` rows of 128 16-bit
 // elements, box 64 x 16, 128-byte swizzle (one 16-token page half per box).
 bool get_pool_tmap(const void* pool, uint64_t rows, int dtype, CUtensorMap* out);
+
+// Validates a bl_head_gather descriptor (host side).
+int check_head_gather(const bl_head_gather& g, const char* who);
+
+// Enqueues the cross-rank completion barrier of a head-sharded decode: this
+// rank announces (release, system scope) to every rank that its stores into
+// their gathered buffers are done, then waits -- at most g.timeout_ns, after
+// which BL_DEVERR_TIMEOUT is set in `err` -- until every rank has announced
+// the same epoch to it.  A plain launch: it starts after all earlier work on
+// the stream has completed.
+int launch_peer_barrier(const bl_head_gather& g, int32_t* err, cudaStream_t s);
 
 }  // namespace bl

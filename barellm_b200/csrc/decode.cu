@@ -204,7 +204,7 @@ constexpr float kLog2e = 1.4426950408889634f;
 struct TCArgs {
   const void* q;
   int64_t q_sb, q_sh;
-  void* out;
+  OutTargets out;
   int64_t o_sb, o_sh;
   const int32_t* block_tables;
   int64_t bt_stride;
@@ -490,8 +490,7 @@ __global__ void __launch_bounds__(kThreadsTC) decode_tc_kernel(const TCArgs a,
       const int hq = h * a.g + hd;
       const float val = (L > 0.f) ? O / L : 0.f;
       if (nch <= 1) {
-        T* op = reinterpret_cast<T*>(a.out) + (int64_t)b * a.o_sb + (int64_t)hq * a.o_sh + d;
-        *op = from_f32<T>(val);
+        store_targets<T>(a.out, (int64_t)b * a.o_sb + (int64_t)hq * a.o_sh + d, from_f32<T>(val));
       } else {
         const int64_t slot_u = (int64_t)a.row_base[b] + bc.y;
         if (slot_u < 0 || slot_u >= a.max_units) continue;  // plan overflow, flagged by the plan kernel
@@ -507,7 +506,7 @@ __global__ void __launch_bounds__(kThreadsTC) decode_tc_kernel(const TCArgs a,
 // split-K reduce
 // ---------------------------------------------------------------------------
 struct ReduceArgs {
-  void* out;
+  OutTargets out;
   int64_t o_sb, o_sh;
   const int32_t* seq_lens;
   int32_t bs, chunk_blocks, bt_width, hq, d;
@@ -541,8 +540,8 @@ __global__ void __launch_bounds__(256) decode_reduce_kernel(const ReduceArgs a) 
       num += w * a.ws_o[((base + c) * a.hq + hq) * a.d + d];
       den += w;
     }
-    T* op = reinterpret_cast<T*>(a.out) + (int64_t)b * a.o_sb + (int64_t)hq * a.o_sh + d;
-    *op = from_f32<T>(den > 0.f ? num / den : 0.f);
+    store_targets<T>(a.out, (int64_t)b * a.o_sb + (int64_t)hq * a.o_sh + d,
+                     from_f32<T>(den > 0.f ? num / den : 0.f));
   }
 }
 
@@ -555,7 +554,7 @@ constexpr int kSimtMaxDPL = 8;  // dims per lane -> head_dim <= 256
 struct SimtArgs {
   const void* q;
   int64_t q_sb, q_sh;
-  void* out;
+  OutTargets out;
   int64_t o_sb, o_sh;
   const void* k_pool;
   const void* v_pool;
@@ -632,7 +631,7 @@ __global__ void __launch_bounds__(kSimtWarps * 32) decode_simt_kernel(const Simt
   __syncthreads();
   float M = -INFINITY;
   for (int w = 0; w < kSimtWarps; ++w) M = fmaxf(M, s_m[w]);
-  T* op = reinterpret_cast<T*>(a.out) + (int64_t)b * a.o_sb + (int64_t)hq * a.o_sh;
+  const int64_t o_row = (int64_t)b * a.o_sb + (int64_t)hq * a.o_sh;
   for (int d = threadIdx.x; d < a.d; d += blockDim.x) {
     float L = 0.f, O = 0.f;
     for (int w = 0; w < kSimtWarps; ++w) {
@@ -640,7 +639,7 @@ __global__ void __launch_bounds__(kSimtWarps * 32) decode_simt_kernel(const Simt
       L += f * s_l[w];
       O += f * s_o[w][d];
     }
-    op[d] = from_f32<T>(L > 0.f ? O / L : 0.f);
+    store_targets<T>(a.out, o_row + d, from_f32<T>(L > 0.f ? O / L : 0.f));
   }
 }
 
@@ -661,7 +660,7 @@ size_t tc_smem_bytes(int g) {
 }
 
 template <typename T>
-int launch_tc_attention(const bl_decode_args& a, const WsLayout& w, cudaStream_t s) {
+int launch_tc_attention(const bl_decode_args& a, const OutTargets& ot, const WsLayout& w, cudaStream_t s) {
   const int g = (int)(a.num_q_heads / a.kv.num_kv_heads);
   const size_t smem = tc_smem_bytes(g);
   static int occ_cache[9] = {0};
@@ -693,7 +692,7 @@ int launch_tc_attention(const bl_decode_args& a, const WsLayout& w, cudaStream_t
   k.q = a.q;
   k.q_sb = a.q_stride_b;
   k.q_sh = a.q_stride_h;
-  k.out = a.out;
+  k.out = ot;
   k.o_sb = a.out_stride_b;
   k.o_sh = a.out_stride_h;
   k.block_tables = a.kv.block_tables;
@@ -728,10 +727,10 @@ int launch_tc_attention(const bl_decode_args& a, const WsLayout& w, cudaStream_t
 }
 
 template <typename T>
-int launch_tc_reduce(const bl_decode_args& a, const WsLayout& w, cudaStream_t s) {
+int launch_tc_reduce(const bl_decode_args& a, const OutTargets& ot, const WsLayout& w, cudaStream_t s) {
   char* ws = (char*)a.workspace;
   ReduceArgs r;
-  r.out = a.out;
+  r.out = ot;
   r.o_sb = a.out_stride_b;
   r.o_sh = a.out_stride_h;
   r.seq_lens = a.seq_lens;
@@ -753,12 +752,12 @@ int launch_tc_reduce(const bl_decode_args& a, const WsLayout& w, cudaStream_t s)
 }
 
 template <typename T>
-int launch_simt(const bl_decode_args& a, cudaStream_t s) {
+int launch_simt(const bl_decode_args& a, const OutTargets& ot, cudaStream_t s) {
   SimtArgs k;
   k.q = a.q;
   k.q_sb = a.q_stride_b;
   k.q_sh = a.q_stride_h;
-  k.out = a.out;
+  k.out = ot;
   k.o_sb = a.out_stride_b;
   k.o_sh = a.out_stride_h;
   k.k_pool = a.kv.k_pool;
@@ -870,36 +869,48 @@ bool is_tc(const bl_decode_args& a) {
 }  // namespace
 }  // namespace bl
 
-extern "C" int bl_paged_decode_attention(const bl_decode_args* args, void* stream) {
-  int rc = check_decode(args, "bl_paged_decode_attention");
-  if (rc) return rc;
-  const bl_decode_args& a = *args;
-  cudaStream_t s = (cudaStream_t)stream;
+namespace bl {
+namespace {
+
+// The attention kernel of a checked call, storing to `ot`.
+int decode_attention(const bl_decode_args& a, const OutTargets& ot, cudaStream_t s) {
   if (is_tc(a)) {
     WsLayout w;
-    rc = check_tc(a, w);
+    const int rc = check_tc(a, w);
     if (rc) return rc;
-    if (a.kv.dtype == BL_BF16) return launch_tc_attention<__nv_bfloat16>(a, w, s);
-    return launch_tc_attention<__half>(a, w, s);
+    if (a.kv.dtype == BL_BF16) return launch_tc_attention<__nv_bfloat16>(a, ot, w, s);
+    return launch_tc_attention<__half>(a, ot, w, s);
   }
   switch (a.kv.dtype) {
-    case BL_F32: return launch_simt<float>(a, s);
-    case BL_F16: return launch_simt<__half>(a, s);
-    default: return launch_simt<__nv_bfloat16>(a, s);
+    case BL_F32: return launch_simt<float>(a, ot, s);
+    case BL_F16: return launch_simt<__half>(a, ot, s);
+    default: return launch_simt<__nv_bfloat16>(a, ot, s);
   }
 }
 
-extern "C" int bl_paged_decode_reduce(const bl_decode_args* args, void* stream) {
-  int rc = check_decode(args, "bl_paged_decode_reduce");
-  if (rc) return rc;
-  const bl_decode_args& a = *args;
+// The split-K reduce of a checked call, storing to `ot`.
+int decode_reduce(const bl_decode_args& a, const OutTargets& ot, cudaStream_t s) {
   if (!is_tc(a)) return BL_OK;  // the SIMT path never splits
   WsLayout w;
-  rc = check_tc(a, w);
+  const int rc = check_tc(a, w);
   if (rc) return rc;
-  cudaStream_t s = (cudaStream_t)stream;
-  if (a.kv.dtype == BL_BF16) return launch_tc_reduce<__nv_bfloat16>(a, w, s);
-  return launch_tc_reduce<__half>(a, w, s);
+  if (a.kv.dtype == BL_BF16) return launch_tc_reduce<__nv_bfloat16>(a, ot, w, s);
+  return launch_tc_reduce<__half>(a, ot, w, s);
+}
+
+}  // namespace
+}  // namespace bl
+
+extern "C" int bl_paged_decode_attention(const bl_decode_args* args, void* stream) {
+  const int rc = check_decode(args, "bl_paged_decode_attention");
+  if (rc) return rc;
+  return decode_attention(*args, one_target(args->out), (cudaStream_t)stream);
+}
+
+extern "C" int bl_paged_decode_reduce(const bl_decode_args* args, void* stream) {
+  const int rc = check_decode(args, "bl_paged_decode_reduce");
+  if (rc) return rc;
+  return decode_reduce(*args, one_target(args->out), (cudaStream_t)stream);
 }
 
 extern "C" int bl_paged_decode(const bl_decode_args* args, void* stream) {
@@ -979,4 +990,40 @@ extern "C" int bl_paged_decode_noalloc(const bl_decode_args* args, void* stream)
   // every entry the attention and reduce kernels read.
   a.plan_ready = 0;
   return bl_paged_decode(&a, stream);
+}
+
+// ---------------------------------------------------------------------------
+// KV-head-sharded decode with the output all-gather fused into the epilogue
+// ---------------------------------------------------------------------------
+// Each rank runs the ordinary plan / attention / reduce over its own heads;
+// the only difference is the output: every element goes to all ranks'
+// gathered buffers at this rank's head offset (rank r + j first, so the
+// ranks do not all write to the same peer at once), and a barrier kernel
+// closes the call.
+extern "C" int bl_paged_decode_allgather(const bl_decode_args* args, const bl_head_gather* gather, void* stream) {
+  const char* who = "bl_paged_decode_allgather";
+  BL_CHECK_ARG(args != nullptr && gather != nullptr, "%s: null argument", who);
+  int rc = check_head_gather(*gather, who);
+  if (rc) return rc;
+  const bl_head_gather& g = *gather;
+  bl_decode_args a = *args;
+  const int es = elem_size(a.kv.dtype);
+  BL_CHECK_ARG(es > 0, "%s: unsupported dtype code %d", who, a.kv.dtype);
+  const int64_t head_bytes = g.head_offset * a.out_stride_h * es;
+  a.out = (char*)g.peer_out[g.rank] + head_bytes;
+  rc = check_decode(&a, who);
+  if (rc) return rc;
+  OutTargets ot = {};
+  ot.n = g.world;
+  for (int j = 0; j < g.world; ++j) ot.ptr[j] = (char*)g.peer_out[(g.rank + j) % g.world] + head_bytes;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (is_tc(a) && !a.plan_ready) {
+    rc = bl_paged_decode_plan(&a, stream);
+    if (rc) return rc;
+  }
+  rc = decode_attention(a, ot, s);
+  if (rc) return rc;
+  rc = decode_reduce(a, ot, s);
+  if (rc) return rc;
+  return launch_peer_barrier(g, a.err, s);
 }

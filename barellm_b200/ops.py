@@ -9,6 +9,7 @@ or without the built library, every call raises.
 
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
@@ -527,6 +528,31 @@ def paged_decode_noalloc(
     a.err = _ptr(err)
     _raise_rc(nat.load().bl_paged_decode_noalloc(a, _stream(q3.device)))
     return out
+
+
+def ipc_export(t: torch.Tensor) -> bytes:
+    """Handle (72 bytes) that lets another process of this node map ``t``'s
+    memory with :func:`ipc_import` (CUDA IPC; ``t`` must stay alive)."""
+    _require_cuda(t, "t")
+    h = nat.IpcHandle()
+    _raise_rc(nat.load().bl_ipc_export(t.data_ptr(), ctypes.byref(h)))
+    return bytes(h)
+
+
+def ipc_import(handle: bytes, device: torch.device) -> int:
+    """Maps memory exported by another process into this one, for ``device``;
+    returns the address that matches the exporter's tensor pointer."""
+    _check(len(handle) == ctypes.sizeof(nat.IpcHandle), "not a bl_ipc_handle")
+    h = nat.IpcHandle.from_buffer_copy(handle)
+    ptr = ctypes.c_void_p()
+    with torch.cuda.device(device):
+        _raise_rc(nat.load().bl_ipc_import(ctypes.byref(h), ctypes.byref(ptr)))
+    return int(ptr.value)
+
+
+def ipc_close(ptr: int) -> None:
+    """Unmaps an address returned by :func:`ipc_import`."""
+    _raise_rc(nat.load().bl_ipc_close(ptr))
 
 
 def paged_prefill(

@@ -49,6 +49,12 @@ WORKLOADS = {
     # across the GPUs, lengths log-uniform 1k..32k, ~150 GB KV pool per GPU
     "decode_qwen8b_long": dict(hq=32, hkv=8, d=128, bs=16, batch=256, len_lo=1024, len_hi=32768, log_uniform=True,
                                pool_bytes=150e9, shard_batch=True, scale=1.0),
+    # the same long-context batch with its KV heads (not its requests) split
+    # across the GPUs: every GPU reads 1/N of every request's K/V and the
+    # per-head outputs are all-gathered by the decode kernels' own stores
+    "decode_qwen8b_long_heads": dict(kind="heads", hq=32, hkv=8, d=128, bs=16, batch=256, len_lo=1024,
+                                     len_hi=32768, log_uniform=True, shard_batch=False, scale=1.0,
+                                     scaling="strong"),
     # paged chunked prefill at Qwen3-8B attention shapes: 32 requests, each a
     # paged prefix of U{0..8192} tokens plus a new chunk of U{512..2048}
     "prefill_qwen8b": dict(kind="prefill", hq=32, hkv=8, d=128, bs=16, batch=32, prefix_lo=0, prefix_hi=8192,
@@ -608,7 +614,7 @@ def run_reference(args, wl_name: str) -> None:
         "warmup": args.warmup,
         "ms_per_step": el * 1e3 / args.steps,
         "higher_is_better": True,
-        "scaling": "strong" if wl["shard_batch"] else "weak",
+        "scaling": wl.get("scaling", "strong" if wl["shard_batch"] else "weak"),
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic",
@@ -618,6 +624,271 @@ def run_reference(args, wl_name: str) -> None:
         "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(res), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# KV-head-sharded decode
+# ---------------------------------------------------------------------------
+class HeadShardWorkload:
+    """One GPU's head shard of a decode batch: every request, but only KV heads
+    [r*Hkv/N, (r+1)*Hkv/N) in this GPU's pool (and the query heads that read
+    them).  Block tables are the same on every GPU."""
+
+    def __init__(self, wl: dict, rank: int, world: int, device: torch.device, seed: int = 1234):
+        from barellm_b200 import head_shard as hs
+        from barellm_b200 import ops
+
+        self.wl, self.device, self.world = wl, device, world
+        self.lens = [int(x) for x in request_lengths(wl, seed)]
+        b = self.batch = len(self.lens)
+        hq, hkv, d, bs = wl["hq"], wl["hkv"], wl["d"], wl["bs"]
+        self.kv0, self.kv1 = hs.kv_head_range(hkv, world, rank)
+        self.q0, self.q1 = hs.q_head_range(hq, hkv, world, rank)
+        hkv_l, hq_l = self.kv1 - self.kv0, self.q1 - self.q0
+        rs = np.random.RandomState(seed)
+        need = [-(-(n + 1) // bs) for n in self.lens]
+        self.pool_blocks = int(sum(need) * 1.25) + 64
+        free = list(rs.permutation(self.pool_blocks))
+        tables = [[int(free.pop()) for _ in range(k)] for k in need]
+        bt = np.full((b, max(need)), -1, dtype=np.int32)
+        for i, t in enumerate(tables):
+            bt[i, : len(t)] = t
+        self.bt = torch.from_numpy(bt).to(device)
+        shape = (1, self.pool_blocks, hkv_l, bs, d)
+        self.k_cache = torch.empty(shape, dtype=torch.bfloat16, device=device)
+        self.v_cache = torch.empty(shape, dtype=torch.bfloat16, device=device)
+        gen = torch.Generator(device=device)
+        gen.manual_seed(seed + 7919 * (rank + 1))
+        sc = wl["scale"]
+        zeros = torch.zeros(b, dtype=torch.int32, device=device)
+        lo = 0
+        while lo < b:
+            hi, tok = lo, 0
+            while hi < b and (tok + self.lens[hi]) * hkv_l * d * 2 <= (1 << 30):
+                tok += self.lens[hi]
+                hi += 1
+            hi = max(hi, lo + 1)
+            n = sum(self.lens[lo:hi])
+            kh = (torch.randn((1, hkv_l, n, d), generator=gen, device=device) * sc).to(torch.bfloat16)
+            vh = (torch.randn((1, hkv_l, n, d), generator=gen, device=device) * sc).to(torch.bfloat16)
+            offs = torch.tensor(np.concatenate([[0], np.cumsum(self.lens[lo:hi])]), dtype=torch.int32, device=device)
+            ops.paged_append(self.k_cache, self.v_cache, 0, self.bt[lo:hi], zeros[lo:hi], kh, vh,
+                             new_offsets=offs, max_new_tokens=max(self.lens[lo:hi]))
+            del kh, vh
+            lo = hi
+        self.q = (torch.randn((b, hq_l, 1, d), generator=gen, device=device) * sc).to(torch.bfloat16)
+        self.k_new = (torch.randn((b, hkv_l, 1, d), generator=gen, device=device) * sc).to(torch.bfloat16)
+        self.v_new = (torch.randn((b, hkv_l, 1, d), generator=gen, device=device) * sc).to(torch.bfloat16)
+        self.starts = torch.tensor(self.lens, dtype=torch.int32, device=device)
+        self.seq_lens_host = [n + 1 for n in self.lens]
+        self.seq_lens = torch.tensor(self.seq_lens_host, dtype=torch.int32, device=device)
+        self.max_seq = max(self.seq_lens_host)
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        self.out_local = torch.empty((b, hq_l, d), dtype=torch.bfloat16, device=device)
+        self.ws = ops.workspace(device, ops.decode_workspace_bytes(b, hq_l, d, bs, self.max_seq))
+        self.shard = hs.HeadShardedDecode(b, hq, hkv, d, torch.bfloat16, device)
+        torch.cuda.synchronize(device)
+
+    def local_bytes(self) -> int:
+        """This GPU's algorithmic bytes: its heads' K/V of every row, its q
+        heads and their outputs."""
+        wl = self.wl
+        hkv_l, hq_l = self.kv1 - self.kv0, self.q1 - self.q0
+        return sum(self.seq_lens_host) * hkv_l * wl["d"] * 2 * 2 + 2 * self.batch * hq_l * wl["d"] * 2
+
+    def step(self) -> torch.Tensor:
+        """append -> plan -> attention -> reduce (outputs stored into every
+        GPU's gathered buffer) -> completion barrier: 5 launches."""
+        from barellm_b200 import ops
+
+        ops.paged_append(self.k_cache, self.v_cache, 0, self.bt, self.starts, self.k_new, self.v_new, err=self.err)
+        return self.shard.decode(self.q, self.k_cache, self.v_cache, 0, self.bt, self.seq_lens, self.max_seq,
+                                 ws=self.ws, err=self.err)
+
+    def step_collective(self) -> torch.Tensor:
+        """The unfused baseline: the same append and decode into a local
+        buffer, then the all-gather through NCCL and a transpose copy."""
+        from barellm_b200 import head_shard as hs
+        from barellm_b200 import ops
+
+        ops.paged_append(self.k_cache, self.v_cache, 0, self.bt, self.starts, self.k_new, self.v_new, err=self.err)
+        ops.paged_decode(self.q, self.k_cache, self.v_cache, 0, self.bt, self.seq_lens, self.max_seq,
+                         out=self.out_local, ws=self.ws, err=self.err)
+        return hs.gather_heads_collective(self.out_local)
+
+    def attention(self) -> None:
+        from barellm_b200 import ops
+
+        ops.paged_decode(self.q, self.k_cache, self.v_cache, 0, self.bt, self.seq_lens, self.max_seq,
+                         out=self.out_local, ws=self.ws, plan_ready=True, err=self.err, stage="attention")
+
+
+def capture(fn, device) -> torch.cuda.CUDAGraph:
+    fn()
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    stream = torch.cuda.Stream(device)
+    stream.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(graph, stream=stream):
+            fn()
+    torch.cuda.current_stream(device).wait_stream(stream)
+    torch.cuda.synchronize(device)
+    return graph
+
+
+def run_heads(args, wl_name: str) -> None:
+    from barellm_b200 import ops
+
+    rank, world, local = dist_env()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    wl = WORKLOADS[wl_name]
+    work = HeadShardWorkload(wl, rank, world, device)
+    steps, warmup = args.steps, args.warmup
+    hq, d = wl["hq"], wl["d"]
+
+    graph = capture(work.step, device)
+    sampler = ClockSampler(local)
+    barrier(world, device)
+    with sampler:
+        for _ in range(warmup):
+            graph.replay()
+        ms = time_steps(graph.replay, steps, device)
+    barrier(world, device)
+    if int(work.err.item()):
+        raise RuntimeError(f"device error word {int(work.err.item())}")
+    ms_max = allreduce(ms, "max", world, device)
+    bytes_step = allreduce(float(work.local_bytes()), "sum", world, device)
+    value = bytes_step * steps / (ms_max / 1e3) / 1e9
+    del graph
+
+    # the unfused baseline: decode, then NCCL all-gather + transpose (graph
+    # captured when there is something to gather)
+    coll_graph = capture(work.step_collective, device) if world > 1 else None
+    run_coll = coll_graph.replay if coll_graph is not None else work.step_collective
+    barrier(world, device)
+    for _ in range(warmup):
+        run_coll()
+    coll_ms = time_steps(run_coll, steps, device)
+    barrier(world, device)
+    coll_ms_max = allreduce(coll_ms, "max", world, device)
+    del coll_graph
+
+    # dominant kernel alone: this GPU's decode attention kernel
+    for _ in range(3):
+        work.attention()
+    n_att = max(steps, 20)
+    att_ms = time_steps(work.attention, n_att, device) / n_att
+    hbm_peak, peak_src = load_peaks()
+    att_bytes = work.local_bytes()
+    achieved = att_bytes / (att_ms / 1e3) / 1e9
+    traffic, traffic_note = traffic_from_profile("decode_tc_kernel", "decode_qwen8b_long", att_bytes)
+
+    # end to end through the public API: this GPU's q / new K / new V heads
+    # from pinned host memory, append + sharded decode, the gathered
+    # [B, Hq, D] output back to the host
+    q_h = work.q.cpu().pin_memory()
+    k_h = work.k_new.cpu().pin_memory()
+    v_h = work.v_new.cpu().pin_memory()
+    out_h = torch.empty((work.batch, hq, d), dtype=torch.bfloat16).pin_memory()
+    q_d, k_d, v_d = torch.empty_like(work.q), torch.empty_like(work.k_new), torch.empty_like(work.v_new)
+
+    def e2e_step():
+        q_d.copy_(q_h, non_blocking=True)
+        k_d.copy_(k_h, non_blocking=True)
+        v_d.copy_(v_h, non_blocking=True)
+        ops.paged_append(work.k_cache, work.v_cache, 0, work.bt, work.starts, k_d, v_d, err=work.err)
+        out = work.shard.decode(q_d, work.k_cache, work.v_cache, 0, work.bt, work.seq_lens, work.max_seq,
+                                ws=work.ws, err=work.err)
+        out_h.copy_(out, non_blocking=True)
+
+    barrier(world, device)
+    for _ in range(warmup):
+        e2e_step()
+    e2e_ms = time_steps(e2e_step, steps, device)
+    barrier(world, device)
+    e2e_ms_max = allreduce(e2e_ms, "max", world, device)
+    e2e_value = bytes_step * steps / (e2e_ms_max / 1e3) / 1e9
+    if int(work.err.item()):
+        raise RuntimeError(f"device error word {int(work.err.item())}")
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        lens = cpu_sample_lens(work.lens, 8, 20000)
+        gbs, runs, per = cpu_run(wl, lens, seconds=args.cpu_seconds, min_runs=1, threads=threads)
+        cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+               "sample": f"{len(lens)} of {work.batch} requests ({sum(lens)} cached tokens), "
+                         f"{runs} runs of {per:.3f} s, float32 numpy restatement of the reference decode chain, "
+                         "threaded over rows"}
+    work.shard.close()
+    if rank == 0:
+        res = {
+            "metric": "paged-decode KV read GB/s",
+            "value": round(value, 2),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": steps,
+            "warmup": warmup,
+            "ms_per_step": ms_max / steps,
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic",
+            "config": {
+                "workload": wl_name,
+                "model_shapes": f"{hq}q/{wl['hkv']}kv heads, head_dim {d}, block_size {wl['bs']}",
+                "requests_total": work.batch,
+                "lengths": f"log-uniform {wl['len_lo']}..{wl['len_hi']}",
+                "kv_heads_per_gpu": work.kv1 - work.kv0,
+                "pool_blocks_per_gpu": work.pool_blocks,
+                "kv_bytes_per_step_per_gpu": work.local_bytes(),
+                "step": "append + plan + decode attention + split-K reduce (outputs stored into every GPU's "
+                        "gathered buffer) + completion barrier, one CUDA graph",
+                "parallelism": f"kv-head shards x{world}, all-gather fused into the decode epilogue (peer stores)",
+                "l2": "inputs larger than L2 (K/V per step per GPU >> 126 MB)",
+            },
+            "hbm_frac_per_gpu": round(value / world / hbm_peak, 4),
+            "collective_baseline": {
+                "value": round(bytes_step * steps / (coll_ms_max / 1e3) / 1e9, 2),
+                "ms_per_step": coll_ms_max / steps,
+                "path": "same decode into a local buffer, then all_gather_into_tensor (NCCL) + transpose copy"
+                        + (", one CUDA graph" if world > 1 else " (nothing to gather at one GPU)"),
+            },
+            "roofline": {
+                "kernel": "decode_tc_kernel",
+                "bound": "hbm",
+                "achieved": round(achieved, 2),
+                "peak": hbm_peak,
+                "peak_source": f"{peak_src} hbm_gbs (copy)",
+                "unit": "GB/s",
+                "frac": round(achieved / hbm_peak, 4),
+                "traffic": traffic,
+                "traffic_note": traffic_note,
+                "algorithmic_bytes_per_launch": att_bytes,
+                "launch_ms": att_ms,
+            },
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": (q_h.numel() + k_h.numel() + v_h.numel()) * 2,
+                    "d2h_bytes_per_step": out_h.numel() * 2, "ms_per_step": e2e_ms_max / steps,
+                    "path": "ops.paged_append + HeadShardedDecode.decode, pinned host I/O per GPU"},
+            "gpu_launches": 5 * steps,
+            "clocks": sampler.summary(),
+        }
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
 
 
 # ---------------------------------------------------------------------------
@@ -1376,6 +1647,9 @@ def main() -> None:
         return
     if kind == "copy":
         (run_reference_copy if args.impl == "reference" else run_copy)(args, args.workload)
+        return
+    if kind == "heads":
+        (run_reference if args.impl == "reference" else run_heads)(args, args.workload)
         return
     if args.impl == "reference":
         (run_reference_prefill if prefill else run_reference)(args, args.workload)

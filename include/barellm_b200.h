@@ -257,6 +257,65 @@ BL_API int bl_paged_decode(const bl_decode_args* args, void* stream);
 BL_API int bl_paged_decode_noalloc(const bl_decode_args* args, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* KV-head-sharded decode: the heads of one decode batch split across the    */
+/* GPUs of a node, the per-head outputs all-gathered over NVLink.            */
+/* The reference runs on one device; its per-head math is the decode chain   */
+/* of SDPAAttentionBackend.attend (src/barellm/attention/backend.py:34-61),  */
+/* which this keeps head for head.  Rank r owns KV heads                     */
+/* [r*Hkv/W, (r+1)*Hkv/W) of every request (its pool holds only those) and   */
+/* the query heads that read them; every rank holds the same block tables.   */
+/*                                                                          */
+/* The all-gather is fused into the attention's epilogue: each output       */
+/* element is stored straight into every rank's gathered buffer (peer       */
+/* memory mapped with bl_ipc_import), then a one-warp barrier publishes     */
+/* completion (st.release.sys into each rank's signal pad) and waits until  */
+/* every rank has done the same (bounded by timeout_ns; BL_DEVERR_TIMEOUT). */
+/* When the call's work has completed on this rank's stream, this rank's    */
+/* gathered buffer holds all Hq heads.  No NCCL, no multicast.              */
+#define BL_MAX_RANKS 8
+
+typedef struct bl_head_gather {
+  int32_t world;                        /* ranks, 1 .. BL_MAX_RANKS            */
+  int32_t rank;                         /* this rank, 0 .. world-1             */
+  void* peer_out[BL_MAX_RANKS];         /* rank r's gathered [batch, Hq, D]    */
+                                        /* buffer as mapped in this process,   */
+                                        /* element (0, 0, 0); strides are      */
+                                        /* args->out_stride_b / _h, the same   */
+                                        /* on every rank                       */
+  int32_t* peer_signal[BL_MAX_RANKS];   /* rank r's signal pad: BL_MAX_RANKS   */
+                                        /* int32 slots, slot s written only by */
+                                        /* rank s; zero before the first call  */
+  int32_t* epoch;                       /* this rank's call counter (device    */
+                                        /* int32, zero before the first call)  */
+  int64_t head_offset;                  /* this rank's first query head in the */
+                                        /* gathered layout                     */
+  int64_t timeout_ns;                   /* bound on the wait; <= 0: 2 s        */
+} bl_head_gather;
+
+/* args describes this rank's shard: q = its query heads [batch, Hq/W, D],
+ * num_q_heads = Hq/W, kv = its pool shard (num_kv_heads = Hkv/W).
+ * args->out is ignored (the outputs go to gather->peer_out).  Every rank
+ * must make the same sequence of calls.  A rank reuses a gathered buffer only
+ * after the next call's barrier, so callers alternate two buffers (or more)
+ * when the output of one call is still being read during the next. */
+BL_API int bl_paged_decode_allgather(const bl_decode_args* args, const bl_head_gather* gather,
+                                     void* stream);
+
+/* Peer mapping of device memory between the processes of one node (CUDA
+ * IPC, no multicast).  export: handle of the allocation holding `ptr` plus
+ * ptr's offset in it.  import: maps that allocation into this process for
+ * the current device and returns the address matching the exporter's ptr.
+ * close: unmaps an address returned by import. */
+typedef struct bl_ipc_handle {
+  unsigned char bytes[64];
+  uint64_t offset;
+} bl_ipc_handle;
+
+BL_API int bl_ipc_export(const void* ptr, bl_ipc_handle* out);
+BL_API int bl_ipc_import(const bl_ipc_handle* handle, void** ptr);
+BL_API int bl_ipc_close(void* ptr);
+
+/* ------------------------------------------------------------------------ */
 /* Prefill attention: causal attention of new query tokens over a paged      */
 /* prefix plus themselves, read in place.                                    */
 /* Replaces the prefill SDPA(is_causal=True) of SDPAAttentionBackend.attend  */
