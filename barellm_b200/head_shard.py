@@ -184,6 +184,8 @@ def gather_heads_collective(out_local: torch.Tensor, group=None) -> torch.Tensor
     import torch.distributed as dist
 
     world, _ = _group_info(group)
+    if world == 1:
+        return out_local
     b, h, d = out_local.shape
     gathered = torch.empty((world * b, h, d), dtype=out_local.dtype, device=out_local.device)
     dist.all_gather_into_tensor(gathered, out_local.contiguous(), group=group)

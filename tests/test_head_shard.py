@@ -190,10 +190,11 @@ class _EmulatedRanks:
         return g
 
 
-def _call(native_lib, st, shard, g):
+def _call(native_lib, st, shard, g, gathered):
+    # ``gathered`` gives the strides of the [B, Hq, D] buffers (the pointer
+    # itself is not used: the outputs go to g.peer_out)
     k, v, q, (q0, q1) = shard
-    a, _, _ = ops._decode_args(q, k, v, 0, st.bt, st.seq_lens, max(st.seq_lens_list), None,
-                               torch.empty(q.shape[0], q1 - q0, q.shape[-1], dtype=q.dtype, device=q.device),
+    a, _, _ = ops._decode_args(q, k, v, 0, st.bt, st.seq_lens, max(st.seq_lens_list), None, gathered[:, q0:q1],
                                None, None, False, st.err)
     rc = native_lib.bl_paged_decode_allgather(ctypes.byref(a), ctypes.byref(g), ops._stream(q.device))
     assert rc == nat.BL_OK, nat.last_error()
@@ -209,13 +210,13 @@ def test_two_ranks_emulated_in_sequence_fill_both_gathered_buffers(cuda, native_
         # rank 0 runs first, so rank 1's announcement for this epoch is
         # written ahead of time; rank 1 then finds rank 0's already there
         em.pad(0)[1] = step
-        _call(native_lib, st, shards[0], em.gather(0, shards[0][3][0]))
+        _call(native_lib, st, shards[0], em.gather(0, shards[0][3][0]), em.outs[0])
         torch.cuda.synchronize()
         assert int(em.pad(1)[0].item()) == step and em.epoch(0) == step
         q0, q1 = shards[0][3]
         for r in range(2):  # rank 0's heads are in both buffers already
             assert torch.equal(em.outs[r][:, q0:q1], ref[:, q0:q1])
-        _call(native_lib, st, shards[1], em.gather(1, shards[1][3][0]))
+        _call(native_lib, st, shards[1], em.gather(1, shards[1][3][0]), em.outs[1])
         torch.cuda.synchronize()
         assert em.epoch(1) == step
         for r in range(2):
@@ -231,7 +232,7 @@ def test_barrier_whose_peer_never_signals_times_out(cuda, native_lib):
     ref = st.decode()
     em = _EmulatedRanks(st, cuda)
     shard = _shard(st, 2, 0)
-    _call(native_lib, st, shard, em.gather(0, 0, timeout_ns=20_000_000))  # nothing writes pad 0 slot 1
+    _call(native_lib, st, shard, em.gather(0, 0, timeout_ns=20_000_000), em.outs[0])  # nothing writes pad 0 slot 1
     torch.cuda.synchronize()
     assert int(st.err.item()) & nat.BL_DEVERR_TIMEOUT
     # the kernel returned; the context still works
