@@ -8,14 +8,16 @@
 // page is fetched once for 256 rows, which halves the K/V bytes per flop of a
 // 128-row tile; keys are consumed in tiles of 128 (8 pages).  Warp roles (12 warps):
 //   warp 0      K producer (one lane): the 8 pages of key tile t as 2-D TMA
-//               boxes (64 x 16, 128-byte swizzle) into a 3-stage K ring; a
+//               boxes (64 x 16, 128-byte swizzle) into a 2-stage K ring; a
 //               page past the row's last page is read at an out-of-range row
 //               coordinate, which TMA fills with zeros.
-//   warps 1..2  V producers: the V pages of tile t-1 into a 2-stage V ring,
-//               16-byte cp.async per thread written in the 128-byte swizzled
-//               layout the MMA reads; slots past the row length are written
-//               as zeros (src-size 0), so stale pool bytes never reach P V.
-//               Each thread's copies arrive on the stage's mbarrier (noinc).
+//   warp 1      V producer: the V pages of tile t-1 into a 3-stage V ring, as
+//               the same TMA boxes (lane 0), except the page holding the
+//               row's last key when the row ends inside it: the 32 lanes copy
+//               it with 16-byte cp.async, zero-filling the slots past the row
+//               length (src-size 0), so stale pool bytes never reach P V.
+//               TMA bytes and the lanes' cp.async arrivals complete the
+//               stage's mbarrier together.  (Warp 2 has no role.)
 //   warp 3      TMEM owner (512 columns: S_A 0..127, S_B 128..255, O_A 256..383,
 //               O_B 384..511) and, on one lane, the MMA issuer.  Per key tile t
 //               it issues O_A += P_A V_{t-1}, S_A = Q_A K_t^T, O_B += P_B V_{t-1},
@@ -45,9 +47,9 @@ constexpr int kKT = 128;                 // keys per tile
 constexpr int kPPT = kKT / kBS;          // 8 pages per tile
 constexpr int kTileRows = 128;           // rows per MMA tile (M)
 constexpr int kRows = 2 * kTileRows;     // score rows per CTA
-constexpr int kKStages = 3;             // K: 3 x 32 KB (K of tile t is read after P V of t-1)
-constexpr int kVStages = 2;
-constexpr int kVProducers = 64;          // threads of warps 1..2 (V by cp.async); warp 0 issues K by TMA
+constexpr int kKStages = 2;             // K: 2 x 32 KB (S of tile t+1 is issued after P V of t-1)
+constexpr int kVStages = 3;             // V: 3 x 32 KB (V is read last, by P V)
+constexpr int kVWarp = 1;
 constexpr int kMmaWarp = 3;
 constexpr int kSoftmaxWarp0 = 4;
 constexpr int kThreads = 384;            // 3 producer warps, MMA warp, 2 x 4 softmax warps
@@ -101,7 +103,7 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, Sh
 
 template <bool BF16>
 __global__ void __launch_bounds__(kThreads, 1)
-    prefill_tc_kernel(const Args a, const __grid_constant__ CUtensorMap kmap) {
+    prefill_tc_kernel(const Args a, const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap) {
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
@@ -135,7 +137,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&sh->empty_k[s], 1);
     }
     for (int s = 0; s < kVStages; ++s) {
-      mbar_init(&sh->full_v[s], kVProducers);
+      mbar_init(&sh->full_v[s], 1 + 32);  // V lane 0's arrive.expect_tx + one cp.async arrival per lane
       mbar_init(&sh->empty_v[s], 1);
     }
     for (int x = 0; x < 2; ++x) {
@@ -192,38 +194,62 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!mbar_wait(&sh->full_k[s], (last / kKStages) & 1)) raise_dev(a.err, BL_DEVERR_TIMEOUT);
         }
       }
-    } else {
-      // V: 8 pages x 16 rows x 16 chunks of 16 bytes per tile; thread vt copies
-      // chunks vt, vt + 64, ... (always chunk vt & 15 of a row); slots past the
-      // row length are zero-filled (src-size 0) so stale pool bytes never
-      // reach P V.  Lanes 0..7 look up the tile's pages, the others shuffle.
-      const int vt = threadIdx.x - 32;
-      const int cc = vt & 15;
-      const uint32_t dst_col = (uint32_t)(cc >> 3) * kHalf;
+    } else if (warp == kVWarp) {
+      // V: the tile's pages as 2-D TMA boxes like K (lane 0), except the page
+      // holding the row's last key when the row ends inside it.  Its slots
+      // past the length may hold stale pool bytes (NaN included), which P V
+      // would turn into NaN even where P = 0, so the warp copies that page
+      // with 16-byte cp.async and zero-fills those slots (src-size 0).  Both
+      // land on the stage's mbarrier: lane 0's arrive.expect_tx for the TMA
+      // bytes plus one cp.async arrival per lane, every tile.
+      const int64_t part_lb = (len % kBS) ? (len - 1) / kBS : -1;
+      if (lane == 0) prefetch_tensormap(&vmap);
       for (int j = 0; j < ntiles; ++j) {
-        const int s = j & 1;
-        if (!wait_or_abort(&sh->empty_v[s], ((j >> 1) & 1) ^ 1, sh, a.err)) break;
+        const int s = j % kVStages;
+        if (!wait_or_abort(&sh->empty_v[s], ((j / kVStages) & 1) ^ 1, sh, a.err)) break;
         unsigned char* stage = smem + kOffV + s * kTile;
-        int phys_l = -1;
-        if (lane < kPPT) {
-          const int lb = j * kPPT + lane;
-          if (lb < npages) {
-            const int64_t ph = bt[lb];
-            if (ph >= 0 && ph < a.num_blocks) phys_l = (int)ph;
+        const int64_t first = (int64_t)j * kPPT;
+        const int pp = (part_lb >= first && part_lb < first + kPPT && part_lb < npages) ? (int)(part_lb - first) : -1;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&sh->full_v[s], (pp >= 0 ? kPPT - 1 : kPPT) * 2 * kBS * 128);
+#pragma unroll 1
+          for (int p = 0; p < kPPT; ++p) {
+            if (p == pp) continue;
+            const int lb = j * kPPT + p;
+            int32_t y = a.rows_total;  // out of range: zeros
+            if (lb < npages) {
+              const int64_t phys = bt[lb];
+              if (phys >= 0 && phys < a.num_blocks) y = (int32_t)(a.layer_row0 + (phys * a.hkv + h) * kBS);
+            }
+            tma_load_2d(stage + p * kBS * 128, &vmap, &sh->full_v[s], 0, y);
+            tma_load_2d(stage + kHalf + p * kBS * 128, &vmap, &sh->full_v[s], 64, y);
           }
         }
-        const int64_t key_t = (int64_t)j * kKT;
-#pragma unroll 4
-        for (int e = vt; e < kPPT * kBS * 16; e += kVProducers) {
-          const int p = e >> 8, r = (e >> 4) & 15;
-          const int phys = __shfl_sync(0xffffffffu, phys_l, p);
-          const uint32_t bytes = (phys >= 0 && key_t + p * kBS + r < len) ? 16u : 0u;
-          const uint16_t* src =
-              a.v_pool + ((a.layer_row0 + ((int64_t)(phys < 0 ? 0 : phys) * a.hkv + h) * kBS + r) * kD + cc * 8);
-          const uint32_t dst = smem_u32(stage + dst_col + (p * kBS + r) * 128 + (((cc & 7) ^ (r & 7)) << 4));
-          asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+        if (pp >= 0) {
+          // 16 rows x 16 chunks of 16 bytes, eight per lane, in the 128-byte
+          // swizzled layout the TMA boxes produce
+          const int64_t lb = first + pp;
+          const int64_t ph = bt[lb];
+          const bool okp = ph >= 0 && ph < a.num_blocks;
+#pragma unroll
+          for (int e = lane; e < kBS * 16; e += 32) {
+            const int r = e >> 4, cc = e & 15;
+            const uint32_t bytes = (okp && lb * kBS + r < len) ? 16u : 0u;
+            const uint16_t* src =
+                a.v_pool + ((a.layer_row0 + ((okp ? ph : 0) * a.hkv + h) * kBS + r) * kD + cc * 8);
+            const uint32_t dst =
+                smem_u32(stage + (cc >> 3) * kHalf + (pp * kBS + r) * 128 + (((cc & 7) ^ (r & 7)) << 4));
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+          }
         }
         asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&sh->full_v[s])) : "memory");
+      }
+      // drain: the V copies in flight land before the CTA can exit
+      if (lane == 0) {
+        for (int s = 0; s < kVStages && s < ntiles; ++s) {
+          const int last = s + ((ntiles - 1 - s) / kVStages) * kVStages;
+          if (!mbar_wait(&sh->full_v[s], (last / kVStages) & 1)) raise_dev(a.err, BL_DEVERR_TIMEOUT);
+        }
       }
     }
     // every copy this thread issued lands before the CTA can exit
@@ -243,12 +269,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t dk0 = umma_desc_sw128(smem_u32(smem + kOffK), 16, 1024);
       const uint64_t dk_stride = (uint64_t)(kTile >> 4);  // one K stage, in 16-byte units
       const uint64_t dv0 = umma_desc_sw128(smem_u32(smem + kOffV), kHalf, 1024);
-      const uint64_t dv1 = umma_desc_sw128(smem_u32(smem + kOffV + kTile), kHalf, 1024);
       // O_X += P_X V_j (P_X in S_X's TMEM columns)
       auto pv = [&](int x, int j) -> bool {
         if (!wait_or_abort(&sh->p_full[x], j & 1, sh, a.err)) return false;
         tc_fence_after();
-        const uint64_t dv = (j & 1) ? dv1 : dv0;
+        const uint64_t dv = dv0 + (uint64_t)(j % kVStages) * (uint64_t)(kTile >> 4);
         const uint32_t d = tmem + kColO + x * 128, pa = tmem + kColS + x * 128;
         tc_mma_ts(d, pa, dv, idesc_o, j > 0 ? 1u : 0u);
 #pragma unroll
@@ -288,16 +313,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       for (int t = 1; t < ntiles && ok; ++t) {
         const int j = t - 1;
-        ok = landed(&sh->full_v[j & 1], (j >> 1) & 1) && pv(0, j) &&
+        ok = landed(&sh->full_v[j % kVStages], (j / kVStages) & 1) && pv(0, j) &&
              landed(&sh->full_k[t % kKStages], (t / kKStages) & 1) && qk(0, t) && pv(1, j);
         if (!ok) break;
-        tc_commit(&sh->empty_v[j & 1]);
+        tc_commit(&sh->empty_v[j % kVStages]);
         if (!(ok = qk(1, t))) break;
         tc_commit(&sh->empty_k[t % kKStages]);
       }
       if (ok && ntiles > 0) {
         const int j = ntiles - 1;
-        ok = landed(&sh->full_v[j & 1], (j >> 1) & 1) && pv(0, j) && pv(1, j);
+        ok = landed(&sh->full_v[j % kVStages], (j / kVStages) & 1) && pv(0, j) && pv(1, j);
       }
       // every MMA issued here has finished before the CTA tears down
       tc_commit(&sh->mma_done);
@@ -490,8 +515,9 @@ int launch(const bl_prefill_args& a, cudaStream_t s) {
   k.layer_row0 = (int64_t)a.kv.layer * a.kv.num_blocks * a.kv.num_kv_heads * kBS;
   k.max_q = a.max_q_len;
   const uint64_t rows = (uint64_t)a.kv.num_layers * a.kv.num_blocks * a.kv.num_kv_heads * kBS;
-  CUtensorMap kmap;
-  if (!get_pool_tmap(a.kv.k_pool, rows, a.kv.dtype, &kmap)) return BL_ERR_LAUNCH;
+  CUtensorMap kmap, vmap;
+  if (!get_pool_tmap(a.kv.k_pool, rows, a.kv.dtype, &kmap) || !get_pool_tmap(a.kv.v_pool, rows, a.kv.dtype, &vmap))
+    return BL_ERR_LAUNCH;
   k.rows_total = (int32_t)rows;
   k.q_vec16 = ((uintptr_t)a.q % 16 == 0) && a.q_stride_b % 8 == 0 && a.q_stride_t % 8 == 0 && a.q_stride_h % 8 == 0;
   k.k_pool = static_cast<const uint16_t*>(a.kv.k_pool);
@@ -500,7 +526,7 @@ int launch(const bl_prefill_args& a, cudaStream_t s) {
   k.err = a.err;
   const int64_t tiles = (a.max_q_len + k.bq - 1) / k.bq;
   dim3 grid((unsigned)tiles, (unsigned)a.kv.num_kv_heads, (unsigned)a.batch);
-  prefill_tc_kernel<BF16><<<grid, kThreads, smem_bytes(), s>>>(k, kmap);
+  prefill_tc_kernel<BF16><<<grid, kThreads, smem_bytes(), s>>>(k, kmap, vmap);
   BL_CHECK_LAUNCH("prefill_tc_kernel");
   return BL_OK;
 }
