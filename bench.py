@@ -779,7 +779,10 @@ def run_heads(args, wl_name: str) -> None:
     coll_ms = time_steps(run_coll, steps, device)
     barrier(world, device)
     coll_ms_max = allreduce(coll_ms, "max", world, device)
-    del coll_graph
+    # the graph holds NCCL work: release it (the bound replay method too)
+    # before the process group is destroyed
+    del run_coll, coll_graph
+    torch.cuda.synchronize(device)
 
     # dominant kernel alone: this GPU's decode attention kernel
     for _ in range(3):
