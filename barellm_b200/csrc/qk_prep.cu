@@ -288,7 +288,7 @@ __device__ __forceinline__ void store_words(T* p, const uint32_t (&w)[E * (int)s
 // in shared memory once (the first rows' loads are issued before that
 // barrier); k / v rows look up their token's pool slot.
 template <typename T, int E, bool VEC>
-__global__ void __launch_bounds__(kWarps * 32, E <= 8 ? 3 : 2) qk_prep_kernel(const PrepArgs a) {
+__global__ void __launch_bounds__(kWarps * 32, E <= 8 ? 4 : 2) qk_prep_kernel(const PrepArgs a) {
   constexpr int D = 16 * E;
   __shared__ __align__(16) T s_rope[2][kTokTile][D];  // cos, sin of the block's tokens
   const int lane = threadIdx.x & 31;
