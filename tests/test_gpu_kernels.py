@@ -297,3 +297,48 @@ def test_packed_chunked_prefill_many_requests(cuda, native_lib, hq, hkv, dtype):
         ref = orc.prefill_attention(qb, kcn, vcn, 0, tables[b], prefix + chunk)
         assert_close_lowp(out[:, :, o : o + chunk], ref)
         o += chunk
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_stale_nan_slots_never_reach_the_outputs(cuda, native_lib, dtype):
+    """The pool starts as NaN everywhere (the reference never clears freed
+    blocks, so a reused slot may hold any bit pattern).  Rows end inside their
+    last page (and one exactly on a page boundary); prefill and decode read
+    those pages in place, and no stale byte may reach an output: P = 0 does
+    not cancel a NaN in P V, so stale V slots must never be loaded."""
+    rs = np.random.RandomState(7)
+    specs = [(0, 45), (37, 130), (300, 17), (16, 200), (513, 64), (100, 28)]
+    hq, hkv, bs, D, P = 32, 8, 16, 128, 512
+    kc = torch.full((1, P, hkv, bs, D), float("nan"), dtype=dtype, device=cuda)
+    vc = torch.full_like(kc, float("nan"))
+    free = list(rs.permutation(P))
+    tables, qs, lens = [], [], []
+    for prefix, chunk in specs:
+        total = prefix + chunk
+        tables.append(np.array([free.pop() for _ in range((total + bs - 1) // bs)], dtype=np.int32))
+        lens.append(total)
+    bt = torch.from_numpy(gh.padded_tables(tables)).to(cuda)
+    gen = torch.Generator().manual_seed(7)
+    for b, (prefix, chunk) in enumerate(specs):
+        k = torch.randn(1, hkv, prefix + chunk, D, generator=gen).to(dtype).to(cuda)
+        v = torch.randn(1, hkv, prefix + chunk, D, generator=gen).to(dtype).to(cuda)
+        ops.paged_append(kc, vc, 0, bt[b : b + 1], torch.tensor([0], dtype=torch.int32, device=cuda), k, v)
+        qs.append(torch.randn(1, hq, chunk, D, generator=gen).to(dtype).to(cuda))
+    q = torch.cat(qs, dim=2)
+    offs = torch.tensor(np.concatenate([[0], np.cumsum([c for _, c in specs])]), dtype=torch.int32, device=cuda)
+    seq = torch.tensor(lens, dtype=torch.int32, device=cuda)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    out = ops.paged_prefill(q, kc, vc, 0, bt, seq, q_offsets=offs, max_q_len=max(c for _, c in specs), err=err)
+    qd = torch.randn(len(specs), hq, 1, D, generator=gen).to(dtype).to(cuda)
+    dec = ops.paged_decode(qd, kc, vc, 0, bt, seq, max(lens), err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    out, dec = out.float().cpu().numpy(), dec.float().cpu().numpy()
+    assert np.isfinite(out).all() and np.isfinite(dec).all()
+    kcn, vcn = kc.float().cpu().numpy(), vc.float().cpu().numpy()
+    o = 0
+    for b, (prefix, chunk) in enumerate(specs):
+        qb = q[:, :, o : o + chunk].float().cpu().numpy()
+        assert_close_lowp(out[:, :, o : o + chunk], orc.prefill_attention(qb, kcn, vcn, 0, tables[b], prefix + chunk))
+        o += chunk
+    assert_close_lowp(dec, orc.decode_attention(qd.float().cpu().numpy(), kcn, vcn, 0, tables, lens)[:, :, 0])
