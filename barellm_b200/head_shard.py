@@ -96,7 +96,9 @@ class HeadShardedDecode:
         self._bases[self.rank] = self.region.data_ptr()
         if self.world > 1:
             handles: list[bytes | None] = [None] * self.world
-            dist.all_gather_object(handles, ops.ipc_export(self.region), group=group)
+            # over NCCL the object exchange stages through the current device
+            with torch.cuda.device(self.device):
+                dist.all_gather_object(handles, ops.ipc_export(self.region), group=group)
             for r in range(self.world):
                 if r != self.rank:
                     self._bases[r] = ops.ipc_import(handles[r], self.device)
