@@ -32,6 +32,10 @@
 // pipeline.)
 //   decode_simt_kernel      any dtype / head_dim <= 256 / block_size / group:
 //                           one CTA per (row, q-head), no split.
+// Every kernel that writes the output stores each element through a short
+// list of targets: the caller's buffer, or -- for the KV-head-sharded decode
+// (bl_paged_decode_allgather, bottom of this file) -- every rank's gathered
+// buffer in peer memory, so the all-gather rides on the epilogue's stores.
 // Roofline: HBM.  Algorithmic bytes per launch = sum_b len_b * Hkv * D * 2 * E
 // (K and V) + 2 * B * Hq * D * E (q, out).
 #include <mutex>
