@@ -2,7 +2,10 @@
 """Paged-decode benchmark: append + split-K decode attention, read in place.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload decode_qwen06b_b64|decode_qwen8b_long]
+                    [--workload NAME]   (default decode_qwen06b_b64; see WORKLOADS:
+                    decode_qwen8b_long, decode_qwen8b_long_heads, prefill_qwen8b,
+                    append_qwen8b_chunks, qkprep_qwen8b_chunks, gather_qwen06b_b64,
+                    e2e_qwen06b)
 
 One step is one pass of the hot path over one batch: the one-token K/V append
 of every request, the split-K plan, the decode attention kernel and the
