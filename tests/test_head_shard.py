@@ -62,6 +62,15 @@ def test_head_ranges_reject_bad_worlds():
         hs.q_head_range(12, 8, 2, 0)
 
 
+def test_head_sharded_decode_rejects_bad_arguments_before_touching_a_device():
+    with pytest.raises(ValueError, match="two buffers"):
+        hs.HeadShardedDecode(2, 16, 8, 128, torch.bfloat16, torch.device("cpu"), buffers=1)
+    with pytest.raises(ValueError, match="unsupported dtype"):
+        hs.HeadShardedDecode(2, 16, 8, 128, torch.int32, torch.device("cpu"))
+    with pytest.raises(ValueError, match="num_heads must divide evenly"):
+        hs.HeadShardedDecode(2, 12, 8, 128, torch.bfloat16, torch.device("cpu"))
+
+
 def _free_port() -> int:
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
