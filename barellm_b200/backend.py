@@ -34,6 +34,16 @@ from .paged_kv_cache import PagedLayerKV, _i32, check
 AttentionBackendName = Literal["auto", "sdpa", "triton", "cuda"]
 
 
+def _paged_rows(layer_cache) -> list[PagedLayerKV] | None:
+    """The member layers of a batched layer view that is not this package's
+    (the reference's BatchLayerKV keeps them in ``.layers``), when every member
+    is a PagedLayerKV of this package; else None."""
+    rows = getattr(layer_cache, "layers", None)
+    if isinstance(rows, list) and rows and all(isinstance(r, PagedLayerKV) for r in rows):
+        return rows
+    return None
+
+
 class AttentionBackend(Protocol):
     def attend(self, q: torch.Tensor, new_k: torch.Tensor, new_v: torch.Tensor, layer_cache,
                group_size: int) -> torch.Tensor: ...
@@ -54,6 +64,12 @@ class CudaPagedAttentionBackend:
             return self._packed_attend(q, layer_cache, layer_cache.append_only(new_k, new_v))
         if layer_cache is None:
             return self._uncached(q, new_k, new_v)
+        rows = _paged_rows(layer_cache)
+        if rows is not None:
+            # the reference's own BatchLayerKV (batched_kv_cache.py:19-26) over
+            # this package's paged layers: the engine's decode batch when only
+            # PagedKVCache and the backend are swapped in
+            return self._batched(q, new_k, new_v, BatchLayerKV(rows))
         raise TypeError(f"the cuda attention backend reads paged caches, not {type(layer_cache).__name__}")
 
     def attend_prepped(self, q: torch.Tensor, new_k: torch.Tensor, new_v: torch.Tensor, q_norm_weight: torch.Tensor,

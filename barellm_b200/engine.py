@@ -218,10 +218,24 @@ class Qwen3(nn.Module):
         return torch.matmul(self.norm(h), self.embed.T)
 
 
-def random_qwen3(shape: Qwen3Shape = QWEN3_06B, dtype=torch.bfloat16, device="cuda", seed: int = 0) -> Qwen3:
+def random_qwen3(shape: Qwen3Shape = QWEN3_06B, dtype=torch.bfloat16, device="cuda", seed: int = 0,
+                 init: str = "spread") -> Qwen3:
+    """A randomly initialised decoder.  ``init="spread"`` (default): token
+    embeddings ~ N(0, 0.02^2) and every projection ~ N(0, 1/fan_in), so the
+    attention and MLP outputs outweigh the token's own embedding in the
+    residual stream and a greedy stream does not collapse onto one repeated
+    token (with nn.Linear's smaller default init the tied head mostly returns
+    the input token).  ``init="default"``: nn.Linear's own init."""
     torch.manual_seed(seed)
     with torch.device("cpu"):
         model = Qwen3(shape)
+        if init == "spread":
+            with torch.no_grad():
+                for m in model.modules():
+                    if isinstance(m, nn.Linear):
+                        m.weight.normal_(0.0, m.weight.shape[1] ** -0.5)
+        elif init != "default":
+            raise ValueError(f"unknown init {init!r}")
     return model.to(device=device, dtype=dtype).eval()
 
 

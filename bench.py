@@ -2,27 +2,33 @@
 """Paged-decode benchmark: append + split-K decode attention, read in place.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload NAME]   (default decode_qwen06b_b64; see WORKLOADS:
-                    decode_qwen8b_long, decode_qwen8b_long_heads, prefill_qwen8b,
+                    [--workload NAME]   (default decode_qwen8b_long; see WORKLOADS:
+                    decode_qwen06b_b64, decode_qwen8b_long_heads, prefill_qwen8b,
                     append_qwen8b_chunks, qkprep_qwen8b_chunks, gather_qwen06b_b64,
                     e2e_qwen06b)
 
 One step is one pass of the hot path over one batch: the one-token K/V append
 of every request, the split-K plan, the decode attention kernel and the
 split-K reduce (4 kernels, replayed as one CUDA graph, each starting early
-through programmatic dependent launch).  Default workload:
-batched paged decode at Qwen3-0.6B attention shapes (16 q / 8 kv heads,
-head_dim 128, block_size 16), bf16, 64 requests per GPU with history lengths
-~U{128..4096}, blocks shuffled across a 65536-block pool, Q/K/V ~ N(0,1)/sqrt(128).
-Multi-GPU runs one process per GPU (torchrun), each with its own BlockPool
-shard and requests (data-parallel by request, no collective on the data path).
+through programmatic dependent launch).  Default workload: long-context
+batched paged decode at Qwen3-8B attention shapes (32 q / 8 kv heads,
+head_dim 128, block_size 16), bf16, one batch of 256 requests with history
+lengths log-uniform in 1k..32k, each GPU's blocks shuffled across a ~150 GB
+pool, Q/K/V ~ N(0,1).  Multi-GPU runs one process per GPU (torchrun), each
+with its own BlockPool shard: the 256 requests are placed whole onto the GPUs
+(longest first onto the least-loaded shard, barellm_b200.placement), so the
+total work is fixed as N grows (strong scaling) and there is no collective on
+the data path.
 
 Metric: algorithmic K/V bytes read per second (sum over GPUs), bytes =
 sum_b len_b * Hkv * D * 2 (K+V) * 2 B  +  q and output bytes.
 
-``--impl reference`` times the reference's own decode chain (append, dense
-gather + pad, repeat_interleave, padding mask, SDPA) restated in float32 numpy
-on this host's cores, on a bounded sample of the same workload.
+``--impl reference`` times the reference's own decode chain (BatchKVCache
+over its PagedKVCache: per-row append, dense gather + pad to the batch's
+longest row, repeat_interleave, padding mask, SDPA through
+SDPAAttentionBackend.attend) from the installed reference package on this
+host's cores, on a bounded sample of the same workload; without the installed
+package it falls back to the float32 numpy restatement of that chain.
 """
 
 from __future__ import annotations
@@ -44,12 +50,16 @@ import torch
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
+from barellm_b200.placement import place_requests  # noqa: E402
+
 WORKLOADS = {
-    # batched paged decode at Qwen3-0.6B attention shapes (the headline workload)
+    # batched paged decode at Qwen3-0.6B attention shapes, 64 requests per GPU
+    # (weak scaling: every GPU decodes a batch with the same 64 lengths)
     "decode_qwen06b_b64": dict(hq=16, hkv=8, d=128, bs=16, batch=64, len_lo=128, len_hi=4096, log_uniform=False,
                                pool_blocks=65536, shard_batch=False, scale=1 / math.sqrt(128)),
-    # long-context decode at Qwen3-8B attention shapes: 256 requests placed
-    # across the GPUs, lengths log-uniform 1k..32k, ~150 GB KV pool per GPU
+    # long-context decode at Qwen3-8B attention shapes (the headline workload):
+    # one batch of 256 requests placed across the GPUs, lengths log-uniform
+    # 1k..32k, ~150 GB KV pool per GPU
     "decode_qwen8b_long": dict(hq=32, hkv=8, d=128, bs=16, batch=256, len_lo=1024, len_hi=32768, log_uniform=True,
                                pool_bytes=150e9, shard_batch=True, scale=1.0),
     # the same long-context batch with its KV heads (not its requests) split
@@ -99,17 +109,6 @@ def request_lengths(wl: dict, seed: int) -> np.ndarray:
     return rs.randint(wl["len_lo"], wl["len_hi"] + 1, size=wl["batch"]).astype(np.int64)
 
 
-def place_requests(lengths: np.ndarray, world: int) -> list[list[int]]:
-    """Scheduler placement across GPUs: longest first onto the least-loaded GPU."""
-    loads = [0] * world
-    out: list[list[int]] = [[] for _ in range(world)]
-    for i in sorted(range(len(lengths)), key=lambda i: -int(lengths[i])):
-        g = min(range(world), key=lambda r: (loads[r], r))
-        out[g].append(i)
-        loads[g] += int(lengths[i])
-    return [sorted(x) for x in out]
-
-
 class DecodeWorkload:
     """Device-resident state of one GPU's share of the workload."""
 
@@ -119,13 +118,15 @@ class DecodeWorkload:
         self.wl = wl
         self.device = device
         if wl["shard_batch"]:
+            # strong scaling: one global batch, whole requests placed on the GPUs
             all_lens = request_lengths(wl, seed)
-            mine = place_requests(all_lens, world)[rank]
-            lens = all_lens[mine]
-            seed_r = seed + 7919 * (rank + 1)
+            self.request_ids = place_requests(all_lens, world)[rank]
+            lens = all_lens[self.request_ids]
         else:
-            seed_r = seed + 7919 * rank
-            lens = request_lengths(wl, seed_r)
+            # weak scaling: every GPU decodes a batch with the same lengths
+            lens = request_lengths(wl, seed)
+            self.request_ids = list(range(len(lens)))
+        seed_r = seed + 7919 * (rank + 1)
         self.lens = [int(x) for x in lens]
         b = len(self.lens)
         self.batch = b
@@ -452,11 +453,189 @@ def cpu_run(wl: dict, lens: list[int], seconds: float, min_runs: int, threads: i
 
 
 # ---------------------------------------------------------------------------
+# the reference's own CPU decode chain (installed copy of the reference)
+# ---------------------------------------------------------------------------
+def reference_package():
+    """The reference's modules from its installed copy (baseline/_ref), or None."""
+    ref = ROOT / "baseline" / "_ref"
+    if not (ref / "barellm" / "engine" / "batched_kv_cache.py").exists():
+        return None
+    if str(ref) not in sys.path:
+        sys.path.append(str(ref))
+    try:
+        from barellm.attention.backend import SDPAAttentionBackend
+        from barellm.engine.batched_kv_cache import BatchKVCache
+        from barellm.engine.block_pool import BlockPool
+        from barellm.engine.kv_cache_manager import KVCacheManager
+        from barellm.engine.paged_kv_cache import PagedKVCache
+    except ImportError:
+        return None
+    import types
+
+    return types.SimpleNamespace(SDPAAttentionBackend=SDPAAttentionBackend, BatchKVCache=BatchKVCache,
+                                 BlockPool=BlockPool, KVCacheManager=KVCacheManager, PagedKVCache=PagedKVCache)
+
+
+class RefDecodeChain:
+    """One layer of the reference's batched decode on host cores, float32 (its
+    CPU dtype): ``BatchKVCache(views).layer(0)`` and
+    ``SDPAAttentionBackend().attend(q, k_new, v_new, layer, group)`` -- the
+    calls Engine._decode -> GroupedQueryAttention.forward make per layer
+    (src/barellm/engine/engine.py:458-488, src/barellm/models/attention.py:171-178):
+    per-row append_only, dense read + zero pad to the batch's longest row,
+    repeat_interleave, padding mask, SDPA.  Every step appends one more token
+    per row, as decoding does.  Blocks come from the reference's BlockPool
+    (free list shuffled by the seed) through its KVCacheManager."""
+
+    def __init__(self, ref, wl: dict, lens: list[int], max_steps: int, seed: int = 5) -> None:
+        hq, hkv, d, bs = wl["hq"], wl["hkv"], wl["d"], wl["bs"]
+        self.wl, self.ref, self.group = wl, ref, hq // hkv
+        gen = torch.Generator().manual_seed(seed)
+        total = [n + max_steps + 1 for n in lens]
+        blocks = sum(-(-t // bs) for t in total)
+        self.kv = ref.PagedKVCache(num_layers=1, max_blocks=blocks, num_kv_heads=hkv, block_size=bs, head_dim=d,
+                                   dtype=torch.float32, device="cpu")
+        pool = ref.BlockPool(blocks)
+        pool.free_ids = [int(x) for x in np.random.RandomState(seed).permutation(blocks)]
+        mgr = ref.KVCacheManager(bs, pool, self.kv)
+
+        class _Req:
+            def __init__(self, rid: str, n: int) -> None:
+                self.id, self.seq_len = rid, n
+
+        reqs = [_Req(f"r{i}", t) for i, t in enumerate(total)]
+        for r in reqs:
+            if not mgr.allocate_request(r):
+                raise RuntimeError("reference block pool too small")
+        self.views = [mgr.get_cache(r) for r in reqs]
+        sc = wl["scale"]
+        for view, n in zip(self.views, lens):
+            k = torch.randn((1, hkv, n, d), generator=gen) * sc
+            v = torch.randn((1, hkv, n, d), generator=gen) * sc
+            view.layer(0).append_only(k, v)
+        b = len(lens)
+        self.q = torch.randn((b, hq, 1, d), generator=gen) * sc
+        self.k_new = torch.randn((b, hkv, 1, d), generator=gen) * sc
+        self.v_new = torch.randn((b, hkv, 1, d), generator=gen) * sc
+        self.backend = ref.SDPAAttentionBackend()
+
+    def step(self) -> int:
+        """One decode step; returns its algorithmic bytes (bf16 element count,
+        the same accounting as the GPU arm)."""
+        layer = self.ref.BatchKVCache(self.views).layer(0)
+        self.backend.attend(self.q, self.k_new, self.v_new, layer, self.group)
+        return cpu_bytes(self.wl, [v.layer(0).seq_len - 1 for v in self.views])
+
+
+def ref_sample_rows(ref, wl: dict, lens: list[int], step_budget_s: float, max_rows: int = 16,
+                    max_padded_tokens: int = 65536) -> list[int]:
+    """The first rows of the workload (at least one) whose reference decode
+    step should take about ``step_budget_s``: one row is timed, and a sample
+    of n rows costs about n x (its longest row) as much per padded token (the
+    reference pads every row to the batch's longest)."""
+    probe = RefDecodeChain(ref, wl, lens[:1], 2)
+    probe.step()
+    t0 = time.perf_counter()
+    probe.step()
+    per_padded = (time.perf_counter() - t0) / max(lens[0], 1)
+    del probe
+    n = 1
+    while n < min(max_rows, len(lens)):
+        m = n + 1
+        padded = m * max(lens[:m])
+        if padded > max_padded_tokens or padded * per_padded > step_budget_s:
+            break
+        n = m
+    return lens[:n]
+
+
+def ref_cpu_run(ref, wl: dict, lens: list[int], seconds: float, min_runs: int, threads: int):
+    """Times the reference's own decode chain; returns (GB/s, runs, sec/run)."""
+    torch.set_num_threads(threads)
+    max_runs = max(min_runs, 1) + 2000  # the pool holds this many appended tokens per row
+    chain = RefDecodeChain(ref, wl, lens, max_runs)
+    with torch.inference_mode():
+        chain.step()  # warm-up
+        t0 = time.perf_counter()
+        runs, nbytes = 0, 0
+        while runs < min_runs or time.perf_counter() - t0 < seconds:
+            nbytes += chain.step()
+            runs += 1
+            if runs + 1 >= max_runs:
+                break
+        el = time.perf_counter() - t0
+    return nbytes / el / 1e9, runs, el / runs
+
+
+def decode_oracle_check(work, out: torch.Tensor, n_rows: int = 3) -> dict:
+    """Checks rows of a decode output against the float64 oracle: the
+    shortest, the longest and a middle row of this GPU's batch, their K/V read
+    back from the pool (bf16 element values).  Raises on a mismatch beyond the
+    bf16 bars (max-abs 2e-2, mean-abs 2e-3)."""
+    from barellm_b200 import ops
+    from oracle import paged_oracle as orc
+
+    lens = work.seq_lens_host
+    order = sorted(range(len(lens)), key=lambda i: lens[i])
+    rows = sorted({order[0], order[-1], order[len(order) // 2]})[:n_rows]
+    k_rows, v_rows = [], []
+    for i in rows:
+        n = lens[i]
+        kd, vd = ops.paged_gather(work.k_cache, work.v_cache, 0, work.bt[i : i + 1],
+                                  torch.tensor([n], dtype=torch.int32, device=work.device), n)
+        k_rows.append(kd[0].float().cpu().numpy())
+        v_rows.append(vd[0].float().cpu().numpy())
+        del kd, vd
+    q = work.q[rows, :, 0].float().cpu().numpy()
+    want = orc.decode_attention_rows(q, k_rows, v_rows)
+    got = out[rows].float().cpu().numpy()
+    err = np.abs(got - want)
+    res = {"rows": [int(r) for r in rows], "row_lengths": [int(lens[r]) for r in rows],
+           "max_abs": float(err.max()), "mean_abs": float(err.mean()), "bars": "max-abs 2e-2, mean-abs 2e-3"}
+    if not (np.isfinite(got).all() and err.max() <= 2e-2 and err.mean() <= 2e-3):
+        raise RuntimeError(f"decode output differs from the oracle: {res}")
+    return res
+
+
+def gather_floats(vals: list[float], world: int, device) -> list[list[float]]:
+    """Every rank's values (all ranks take part), outside any timed region."""
+    if world == 1:
+        return [list(vals)]
+    import torch.distributed as dist
+
+    t = torch.tensor(vals, dtype=torch.float64, device=device)
+    out = torch.empty((world, len(vals)), dtype=torch.float64, device=device)
+    dist.all_gather_into_tensor(out, t)
+    return out.tolist()
+
+
+def cpu_baselines(wl: dict, lens: list[int], batch: int, seconds: float) -> tuple[dict, dict]:
+    """The N=1 rank-0 CPU baselines: the reference's own chain (when its
+    installed copy imports) and the numpy restatement of it."""
+    threads = os.cpu_count() or 1
+    ref = reference_package()
+    primary = None
+    if ref is not None:
+        rlens = ref_sample_rows(ref, wl, lens, step_budget_s=2.0)
+        gbs, runs, per = ref_cpu_run(ref, wl, rlens, seconds=seconds, min_runs=1, threads=threads)
+        primary = {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "reference",
+                   "sample": f"{len(rlens)} of {batch} requests ({sum(rlens)} cached tokens, padded to "
+                             f"{max(rlens)}), {runs} decode steps of {per:.3f} s: the reference's "
+                             "BatchKVCache + SDPAAttentionBackend.attend on its PagedKVCache, float32, "
+                             f"torch.set_num_threads({threads})"}
+    plens = cpu_sample_lens(lens, 8, 20000)
+    gbs, runs, per = cpu_run(wl, plens, seconds=seconds / 2 if primary else seconds, min_runs=1, threads=threads)
+    port = {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{len(plens)} of {batch} requests ({sum(plens)} cached tokens), {runs} runs of {per:.3f} s, "
+                      "float32 numpy restatement of the reference decode chain, threaded over rows (each group of "
+                      "rows padded to its own longest)"}
+    return (primary or port), (port if primary else None)
+
+
+# ---------------------------------------------------------------------------
 # arms
 # ---------------------------------------------------------------------------
 def run_ours(args, wl_name: str) -> None:
-    from barellm_b200 import ops
-
     rank, world, local = dist_env()
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
@@ -494,6 +673,12 @@ def run_ours(args, wl_name: str) -> None:
     ms_max = allreduce(ms, "max", world, device)
     bytes_step = allreduce(float(work.decode_bytes()), "sum", world, device)
     value = bytes_step * steps / (ms_max / 1e3) / 1e9
+    per_gpu = gather_floats([float(work.decode_bytes()), ms / steps, float(work.batch)], world, device)
+
+    # the timed graph's output, checked against the oracle (not timed; every
+    # replay appends the same token at the same position, so the output is
+    # that of one step)
+    oracle_check = decode_oracle_check(work, work.out)
 
     # dominant kernel alone: the decode attention kernel, eager launches
     for _ in range(3):
@@ -503,8 +688,6 @@ def run_ours(args, wl_name: str) -> None:
     att_bytes = work.decode_bytes()
     achieved = att_bytes / (att_ms / 1e3) / 1e9
     traffic, traffic_note = traffic_from_profile("decode_tc_kernel", wl_name, att_bytes)
-
-    # output sanity vs the oracle on a few rows (not timed)
     del graph
 
     # end to end through the public API with host buffers
@@ -514,17 +697,12 @@ def run_ours(args, wl_name: str) -> None:
     e2e_bytes = allreduce(float(e2e["bytes"]), "sum", world, device)
     e2e_value = e2e_bytes / (e2e_ms / 1e3) / 1e9
 
-    cpu = None
+    cpu, cpu_port = None, None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        threads = os.cpu_count() or 1
-        lens = cpu_sample_lens(work_lens, 8, 20000)
-        gbs, runs, per = cpu_run(wl, lens, seconds=args.cpu_seconds, min_runs=1, threads=threads)
-        cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port",
-               "sample": f"{len(lens)} of {work.batch} requests ({sum(lens)} cached tokens), "
-                         f"{runs} runs of {per:.3f} s, float32 numpy restatement of the reference decode chain, "
-                         "threaded over rows"}
+        cpu, cpu_port = cpu_baselines(wl, work_lens, work.batch, args.cpu_seconds)
 
     if rank == 0:
+        kv_bytes = [int(r[0]) for r in per_gpu]
         res = {
             "metric": "paged-decode KV read GB/s",
             "value": round(value, 2),
@@ -547,10 +725,21 @@ def run_ours(args, wl_name: str) -> None:
                 "pool_blocks_per_gpu": work.pool_blocks,
                 "kv_bytes_per_step_per_gpu": work.decode_bytes(),
                 "step": "append + plan + decode attention + split-K reduce, one CUDA graph",
-                "parallelism": f"dp{world} by request (one BlockPool shard per GPU)",
+                "parallelism": (f"dp{world} by request: one batch placed whole-request onto the GPUs' BlockPool "
+                                "shards, longest first onto the least-loaded" if wl["shard_batch"] else
+                                f"dp{world} by request: every GPU decodes its own batch with the same lengths"),
                 "l2": "inputs larger than L2 (K/V per step >> 126 MB)",
             },
             "hbm_frac_per_gpu": round(value / world / hbm_peak, 4),
+            "per_gpu": {
+                "requests": [int(r[2]) for r in per_gpu],
+                "kv_bytes_per_step": kv_bytes,
+                "step_ms": [round(r[1], 5) for r in per_gpu],
+                "bytes_imbalance_max_over_mean": round(max(kv_bytes) / (sum(kv_bytes) / len(kv_bytes)), 4),
+                "note": "value = bytes of all GPUs / the slowest GPU's time; the imbalance bounds the strong-scaling "
+                        "efficiency from above",
+            },
+            "oracle_check": oracle_check,
             "roofline": {
                 "kernel": "decode_tc_kernel",
                 "bound": "hbm",
@@ -565,6 +754,7 @@ def run_ours(args, wl_name: str) -> None:
                 "launch_ms": att_ms,
             },
             "cpu_baseline": cpu,
+            "cpu_baseline_port": cpu_port,
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": e2e["h2d"],
                     "d2h_bytes_per_step": e2e["d2h"], "ms_per_step": e2e_ms / steps,
                     "path": "PagedKVCache + BatchKVCache + CudaPagedAttentionBackend.attend, pinned host I/O"},
@@ -579,7 +769,9 @@ def run_ours(args, wl_name: str) -> None:
 
 
 def run_reference(args, wl_name: str) -> None:
-    """The reference's CPU decode chain, on host cores, bounded per step."""
+    """The reference's CPU decode chain, on host cores, bounded per step: its
+    own classes from the installed copy when they import (else the numpy
+    restatement), on the first rows of the same workload."""
     rank, world, _ = dist_env()
     if rank != 0:
         return
@@ -589,25 +781,44 @@ def run_reference(args, wl_name: str) -> None:
     threads = os.cpu_count() or 1
     # size the per-step sample so the whole run stays within ~2 minutes
     budget = 120.0 / max(args.steps + args.warmup, 1)
-    cand = cpu_sample_lens(all_lens, 8, 20000)
-    _, _, per_row = cpu_run(wl, cand[:1], seconds=0.0, min_runs=1, threads=threads)
-    n_rows = int(max(1, min(len(cand), budget / max(per_row, 1e-6))))
-    lens = cand[:n_rows]
-    from oracle import paged_oracle as orc
+    ref = reference_package()
+    if ref is not None:
+        torch.set_num_threads(threads)
+        lens = ref_sample_rows(ref, wl, all_lens, step_budget_s=budget)
+        chain = RefDecodeChain(ref, wl, lens, args.steps + args.warmup + 1)
+        with torch.inference_mode():
+            for _ in range(args.warmup):
+                chain.step()
+            t0 = time.perf_counter()
+            nbytes = sum(chain.step() for _ in range(args.steps))
+            el = time.perf_counter() - t0
+        kind = "reference"
+        sample = (f"{len(lens)} of {len(all_lens)} requests per step ({sum(lens)} cached tokens, padded to "
+                  f"{max(lens)}): the reference's BatchKVCache + SDPAAttentionBackend.attend on its PagedKVCache "
+                  f"(installed copy), float32, torch.set_num_threads({threads})")
+        dtype = "f32"
+    else:
+        cand = cpu_sample_lens(all_lens, 8, 20000)
+        _, _, per_row = cpu_run(wl, cand[:1], seconds=0.0, min_runs=1, threads=threads)
+        n_rows = int(max(1, min(len(cand), budget / max(per_row, 1e-6))))
+        lens = cand[:n_rows]
+        from oracle import paged_oracle as orc
 
-    kc, vc, tables, lens_a, q, kn, vn = cpu_sample_state(wl, lens)
-    nbytes = cpu_bytes(wl, lens)
-    with ThreadPoolExecutor(threads) as ex:
-        for _ in range(args.warmup):
-            orc.decode_step_cpu(kc, vc, 0, tables, lens_a, q, kn, vn, executor=ex)
-        t0 = time.perf_counter()
-        for _ in range(args.steps):
-            orc.decode_step_cpu(kc, vc, 0, tables, lens_a, q, kn, vn, executor=ex)
-        el = time.perf_counter() - t0
-    value = nbytes * args.steps / el / 1e9
-    sample = (f"{n_rows} of {len(all_lens)} requests per step ({sum(lens)} cached tokens), float32 numpy "
-              "restatement of the reference decode chain (append, gather + pad, repeat_interleave, mask, SDPA), "
-              "threaded over rows")
+        kc, vc, tables, lens_a, q, kn, vn = cpu_sample_state(wl, lens)
+        nbytes = cpu_bytes(wl, lens) * args.steps
+        with ThreadPoolExecutor(threads) as ex:
+            for _ in range(args.warmup):
+                orc.decode_step_cpu(kc, vc, 0, tables, lens_a, q, kn, vn, executor=ex)
+            t0 = time.perf_counter()
+            for _ in range(args.steps):
+                orc.decode_step_cpu(kc, vc, 0, tables, lens_a, q, kn, vn, executor=ex)
+            el = time.perf_counter() - t0
+        kind = "port"
+        sample = (f"{n_rows} of {len(all_lens)} requests per step ({sum(lens)} cached tokens), float32 numpy "
+                  "restatement of the reference decode chain (append, gather + pad, repeat_interleave, mask, SDPA), "
+                  "threaded over rows (the reference's installed copy was not found)")
+        dtype = "f32"
+    value = nbytes / el / 1e9
     res = {
         "metric": "paged-decode KV read GB/s",
         "value": round(value, 4),
@@ -619,11 +830,12 @@ def run_reference(args, wl_name: str) -> None:
         "higher_is_better": True,
         "scaling": wl.get("scaling", "strong" if wl["shard_batch"] else "weak"),
         "vs_baseline": None,
-        "dtype": "f32",
+        "dtype": dtype,
         "data": "synthetic",
-        "config": {"workload": wl_name, "lengths": f"{wl['len_lo']}..{wl['len_hi']}"},
+        "config": {"workload": wl_name, "lengths": f"{wl['len_lo']}..{wl['len_hi']}",
+                   "bytes": "same algorithmic accounting as the GPU arm (bf16 element count of the K/V read)"},
         "impl": "reference",
-        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": kind, "sample": sample},
         "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(res), flush=True)
@@ -825,15 +1037,9 @@ def run_heads(args, wl_name: str) -> None:
     if int(work.err.item()):
         raise RuntimeError(f"device error word {int(work.err.item())}")
 
-    cpu = None
+    cpu, cpu_port = None, None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        threads = os.cpu_count() or 1
-        lens = cpu_sample_lens(work.lens, 8, 20000)
-        gbs, runs, per = cpu_run(wl, lens, seconds=args.cpu_seconds, min_runs=1, threads=threads)
-        cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port",
-               "sample": f"{len(lens)} of {work.batch} requests ({sum(lens)} cached tokens), "
-                         f"{runs} runs of {per:.3f} s, float32 numpy restatement of the reference decode chain, "
-                         "threaded over rows"}
+        cpu, cpu_port = cpu_baselines(wl, list(work.lens), work.batch, args.cpu_seconds)
     work.shard.close()
     if rank == 0:
         res = {
@@ -883,6 +1089,7 @@ def run_heads(args, wl_name: str) -> None:
                 "launch_ms": att_ms,
             },
             "cpu_baseline": cpu,
+            "cpu_baseline_port": cpu_port,
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": (q_h.numel() + k_h.numel() + v_h.numel()) * 2,
                     "d2h_bytes_per_step": out_h.numel() * 2, "ms_per_step": e2e_ms_max / steps,
@@ -1626,7 +1833,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode_qwen06b_b64")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode_qwen8b_long")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--pool-blocks", type=int, default=0,

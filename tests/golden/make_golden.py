@@ -3,10 +3,11 @@
 The reference (quanhua92/barellm) is pure Python on PyTorch and imports on a
 CPU; this script drives its own classes -- PagedKVCache, BlockPool,
 KVCacheManager, BatchKVCache, SDPAAttentionBackend -- on the seeded inputs of
-``cases.py`` and stores their outputs.  It needs the reference source tree
-(``$BARELLM_REFERENCE``, default ``/root/reference``), which only exists in the
-build container, so the fixtures are committed and the tests never import the
-reference.
+``cases.py`` and stores their outputs.  It imports the reference package from
+``$BARELLM_REFERENCE`` when that is set (a source tree whose ``src`` holds the
+package, or a directory holding ``barellm`` itself), else from the installed
+copy under ``baseline/_ref`` at the repository root.  The fixtures are
+committed, so the tests themselves never need the reference.
 
     python tests/golden/make_golden.py
 """
@@ -23,7 +24,8 @@ import torch.nn.functional as F
 
 HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE))
-REF_SRC = Path(os.environ.get("BARELLM_REFERENCE", "/root/reference")) / "src"
+_REF = Path(os.environ.get("BARELLM_REFERENCE", HERE.parents[1] / "baseline" / "_ref"))
+REF_SRC = _REF / "src" if (_REF / "src" / "barellm").is_dir() else _REF
 sys.path.insert(0, str(REF_SRC))
 
 import cases  # noqa: E402

@@ -19,6 +19,7 @@ BASE_KEYS = {"metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_ste
 TINY = {
     # name in WORKLOADS -> overrides that shrink it
     "decode_qwen06b_b64": dict(batch=3, len_lo=20, len_hi=60),
+    "decode_qwen8b_long": dict(batch=3, len_lo=20, len_hi=60),
     "decode_qwen8b_long_heads": dict(batch=3, len_lo=20, len_hi=60),
     "prefill_qwen8b": dict(batch=2, prefix_lo=0, prefix_hi=40, chunk_lo=16, chunk_hi=24),
     "append_qwen8b_chunks": dict(batch=2, prefix_lo=0, prefix_hi=40, chunk_lo=16, chunk_hi=24),
@@ -27,6 +28,7 @@ TINY = {
 }
 GPU_METRIC = {
     "decode_qwen06b_b64": ("paged-decode KV read GB/s", "GB/s"),
+    "decode_qwen8b_long": ("paged-decode KV read GB/s", "GB/s"),
     "decode_qwen8b_long_heads": ("paged-decode KV read GB/s", "GB/s"),
     "prefill_qwen8b": ("paged chunked-prefill attention TFLOP/s", "TFLOP/s"),
 }
@@ -55,7 +57,10 @@ def test_reference_arm_prints_the_contract_line(name, monkeypatch, capsys):
     assert res["config"]["workload"] == name
     cpu = res["cpu_baseline"]
     assert cpu["value"] == res["value"] and cpu["unit"] == res["unit"] and cpu["cores"] >= 1
-    assert cpu["kind"] == "port" and cpu["sample"]
+    assert cpu["kind"] in ("port", "reference") and cpu["sample"]
+    if wl.get("kind") not in ("prefill", "copy"):
+        # the decode arms run the reference's own classes when its installed copy imports
+        assert cpu["kind"] == ("reference" if bench.reference_package() is not None else "port")
     assert res["e2e"] == {"value": res["value"], "unit": res["unit"], "h2d_bytes_per_step": 0,
                           "d2h_bytes_per_step": 0}
     if name in GPU_METRIC:
@@ -70,3 +75,31 @@ def test_reference_arm_is_silent_on_other_ranks(monkeypatch, capsys):
     bench.run_reference_prefill(args, "prefill_qwen8b")
     bench.run_reference_copy(args, "gather_qwen06b_b64")
     assert capsys.readouterr().out == ""
+
+
+def test_reference_chain_computes_what_the_oracle_computes():
+    """The CPU baseline's reference chain (the reference's BatchKVCache +
+    SDPAAttentionBackend on its PagedKVCache) gives, step after step, the
+    oracle's decode attention over the same histories: the baseline times the
+    same computation the GPU arm is checked against."""
+    ref = bench.reference_package()
+    if ref is None:
+        pytest.skip("the reference's installed copy (baseline/_ref) is not present")
+    import numpy as np
+
+    from oracle import paged_oracle as orc
+
+    wl = dict(bench.WORKLOADS["decode_qwen8b_long"], batch=3)
+    lens = [37, 5, 80]
+    chain = bench.RefDecodeChain(ref, wl, lens, 3)
+    for step in range(2):
+        layer = ref.BatchKVCache(chain.views).layer(0)
+        out = chain.backend.attend(chain.q, chain.k_new, chain.v_new, layer, chain.group)
+        k_rows, v_rows = [], []
+        for view in chain.views:
+            k, v = view.layer(0).read()
+            k_rows.append(k[0].numpy())
+            v_rows.append(v[0].numpy())
+        assert [k.shape[1] for k in k_rows] == [n + step + 1 for n in lens]
+        want = orc.decode_attention_rows(chain.q[:, :, 0].numpy(), k_rows, v_rows)
+        np.testing.assert_allclose(out[:, :, 0].numpy(), want, atol=1e-5, rtol=1e-5)

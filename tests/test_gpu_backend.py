@@ -169,6 +169,55 @@ def test_batched_read_pads_unequal_histories(native_lib):
     assert bool((k[0, :, :15] == 1).all()) and bool((v[1] == 102).all())
 
 
+def test_batched_read_and_mask_match_the_reference_golden(native_lib):
+    """The reference's batched read scenario (tests/golden/batch_read.npz,
+    made by its PagedKVCache / KVCacheManager / BatchKVCache: boundary lengths
+    15..33 at block_size 16, two layers, pool pre-filled with a sentinel)
+    replayed call for call through the drop-in classes: same block tables,
+    same pool bytes, same zero-padded reads and the same [B, 1, 1, Tmax]
+    attention mask (batched_kv_cache.py:65-102), element for element."""
+    from pathlib import Path
+
+    import cases
+    from barellm_b200.block_pool import KVCacheBlock  # noqa: F401  (the manager hands these out)
+
+    g = np.load(Path(__file__).resolve().parent / "golden" / "batch_read.npz")
+    lengths = [int(n) for n in g["lengths"]]
+    bs = 16
+    max_blocks = sum(-(-n // bs) for n in lengths)
+    storage = PagedKVCache(2, max_blocks, 2, bs, 3, device=DEV)
+    storage.key_cache.fill_(-7.0)
+    storage.value_cache.fill_(-7.0)
+    mgr = KVCacheManager(bs, BlockPool(max_blocks), storage)
+
+    class R:
+        def __init__(self, rid, n):
+            self.id, self.seq_len = rid, n
+
+    caches = []
+    for i, n in enumerate(lengths):
+        req = R(f"b{i}", n)
+        assert mgr.allocate_request(req)
+        cache = mgr.get_cache(req)
+        for layer in range(2):
+            k = torch.from_numpy(cases.pattern_tensor(i, layer, n, 2, 3, 0.0)).to(DEV)
+            v = torch.from_numpy(cases.pattern_tensor(i, layer, n, 2, 3, 0.5)).to(DEV)
+            cache.layer(layer).append_only(k, v)
+        caches.append(cache)
+    tables = [storage.request_pages[f"b{i}"].block_table.cpu().numpy() for i in range(len(lengths))]
+    np.testing.assert_array_equal(gh.padded_tables(tables, g["block_tables"].shape[1]), g["block_tables"])
+    np.testing.assert_array_equal(storage.key_cache.cpu().numpy(), g["key_cache"])
+    np.testing.assert_array_equal(storage.value_cache.cpu().numpy(), g["value_cache"])
+    for layer in range(2):
+        batch_layer = BatchKVCache(caches).layer(layer)
+        k, v = batch_layer.read()
+        np.testing.assert_array_equal(k.cpu().numpy(), g[f"k{layer}"])
+        np.testing.assert_array_equal(v.cpu().numpy(), g[f"v{layer}"])
+        mask = batch_layer.attention_mask(1)
+        assert mask.dtype == torch.bool and mask.device.type == "cuda"
+        np.testing.assert_array_equal(mask.cpu().numpy(), g[f"mask{layer}"])
+
+
 # ---- the attention backend ---------------------------------------------------------
 def build_requests(lengths, hq, hkv, d, bs, dtype, seed=0, extra=1, max_blocks=None):
     rs = np.random.RandomState(seed)

@@ -4,9 +4,14 @@ against the same weights on the contiguous-cache SDPA oracle.
 
 fp32: greedy tokens identical (the reference checks cached vs uncached and
 batched vs independent decodes at 1e-5: tests/test_generate.py:230-288,
-tests/test_batched_kv_cache.py:92-150).  bf16: identical up to the first
-divergence, and a divergence may only happen where the oracle's top-2 logits
-are a near-tie (bf16 logits round at ~1e-2 here)."""
+tests/test_batched_kv_cache.py:92-150), including at the Qwen3-0.6B
+architecture's full size (28 layers, vocab 151936).  bf16: teacher-forced --
+both runs are fed the oracle's own greedy tokens, and at every step of every
+prompt the paged run's argmax must equal the oracle's, except where the
+oracle's top-2 logits are a near-tie (bf16 logits round at ~1e-2 here); the
+number of such steps is small and reported.  The weights use the "spread"
+random init, whose greedy streams do not collapse onto one repeated token
+(the tests check that)."""
 
 from __future__ import annotations
 
@@ -65,22 +70,98 @@ def test_fp32_uncached_recompute_matches_cached_decode(cuda, native_lib):
     assert cached == toks[len(prompt):]
 
 
-def test_bf16_qwen06b_attention_shapes_match_up_to_near_ties(cuda, native_lib):
+@torch.inference_mode()
+def paged_forced_argmax(model, prompts: list[list[int]], forced: list[list[int]]):
+    """The paged engine fed the given tokens: packed prefill of the prompts,
+    then eager batched decode steps whose inputs are ``forced`` (not the
+    engine's own argmax).  Returns the argmax of every step per prompt."""
+    from barellm_b200 import BatchKVCache
+    from barellm_b200.engine import _Request
+
+    n = len(forced[0])
+    eng = PagedEngine(model, num_blocks=PagedEngine.blocks_needed([len(p) for p in prompts], n, 16) + 4)
+    reqs = [_Request(f"req-{i}", p) for i, p in enumerate(prompts)]
+    for r in reqs:
+        assert eng.manager.allocate_request(r)
+    eng._prefill_packed(reqs)
+    got = [[r.tokens[-1]] for r in reqs]
+    for r, f in zip(reqs, forced):
+        r.tokens[-1] = f[0]
+    dev = eng.device
+    for step in range(1, n):
+        for r in reqs:
+            assert eng.manager.allocate_request(r)
+        ids = torch.tensor([[r.tokens[-1]] for r in reqs], dtype=torch.long, device=dev)
+        pos = torch.tensor([[r.seq_len - 1] for r in reqs], dtype=torch.long, device=dev)
+        logits = model(ids, pos, kv_cache=BatchKVCache([eng.manager.get_cache(r) for r in reqs]))
+        for i, (r, tok) in enumerate(zip(reqs, torch.argmax(logits[:, -1], dim=-1).tolist())):
+            got[i].append(int(tok))
+            r.tokens.append(forced[i][step])
+    eng.cache.check_device_errors()
+    return got
+
+
+def forced_agreement(got, want, margins, tie: float):
+    """Steps where the argmax differs; each must be a near-tie of the oracle."""
+    diffs = [(i, k, margins[i][k]) for i in range(len(want)) for k in range(len(want[i])) if got[i][k] != want[i][k]]
+    bad = [d for d in diffs if d[2] >= tie]
+    return diffs, bad
+
+
+def test_bf16_teacher_forced_every_step_matches_up_to_near_ties(cuda, native_lib):
     shape = Qwen3Shape(vocab_size=2048, num_layers=4)  # Qwen3-0.6B attention/MLP widths, fewer layers
     model = random_qwen3(shape, dtype=torch.bfloat16, device=cuda, seed=5)
     prompts = prompts_for(8, 20, 300, shape.vocab_size, seed=6)
     n_new = 24
+    want, margins = generate_contiguous(model, prompts, n_new, record_margins=True)
+    assert all(len(set(t)) >= 4 for t in want), want  # varied greedy streams
+    got = paged_forced_argmax(model, prompts, want)
+    diffs, bad = forced_agreement(got, want, margins, tie=0.05)
+    assert not bad, f"argmax differs away from a near-tie (prompt, step, oracle top-2 margin): {bad}"
+    assert len(diffs) <= len(prompts) * n_new // 20, diffs
+    # free-running greedy through the engine's CUDA-graph decode agrees with
+    # the oracle up to the first near-tie of every prompt
+    free = PagedEngine(model, num_blocks=PagedEngine.blocks_needed([len(p) for p in prompts], n_new, 16) + 4
+                       ).generate(prompts, max_new_tokens=n_new)
+    for g, w, m in zip(free, want, margins):
+        if g != w:
+            k = next(i for i, (a, b) in enumerate(zip(g, w)) if a != b)
+            assert m[k] < 0.05, f"free-running divergence at step {k}, oracle top-2 margin {m[k]:.4f}"
+
+
+def test_qwen06b_full_architecture_fp32_greedy_identical(cuda, native_lib):
+    """The end-to-end configuration's model at full size (28 layers, hidden
+    1024, 16q/8kv heads, head_dim 128, SwiGLU 3072, vocab 151936, tied head),
+    fp32, a slice of its workload: 12 prompts of U{64..2048} random token ids,
+    24 greedy tokens through the paged engine; identical to the contiguous
+    oracle."""
+    from barellm_b200.engine import QWEN3_06B
+
+    model = random_qwen3(QWEN3_06B, dtype=torch.float32, device=cuda, seed=0)
+    prompts = prompts_for(12, 64, 2048, QWEN3_06B.vocab_size, seed=2024)
+    n_new = 24
     engine = PagedEngine(model, num_blocks=PagedEngine.blocks_needed([len(p) for p in prompts], n_new, 16) + 4)
     got = engine.generate(prompts, max_new_tokens=n_new)
+    want, _ = generate_contiguous(model, prompts, n_new)
+    assert all(len(set(t)) >= 4 for t in want)
+    assert got == want
+
+
+def test_qwen06b_full_architecture_bf16_teacher_forced(cuda, native_lib):
+    """The same full-size model in bf16 (the end-to-end workload's dtype), 32
+    prompts of U{64..2048} tokens, 64 teacher-forced decode steps each: every
+    step's argmax equals the oracle's except at near-ties."""
+    from barellm_b200.engine import QWEN3_06B
+
+    model = random_qwen3(QWEN3_06B, dtype=torch.bfloat16, device=cuda, seed=0)
+    prompts = prompts_for(32, 64, 2048, QWEN3_06B.vocab_size, seed=2024)
+    n_new = 64
     want, margins = generate_contiguous(model, prompts, n_new, record_margins=True)
-    identical = 0
-    for g, w, m in zip(got, want, margins):
-        if g == w:
-            identical += 1
-            continue
-        k = next(i for i, (a, b) in enumerate(zip(g, w)) if a != b)
-        assert m[k] < 0.25, f"divergence at step {k} with oracle top-2 margin {m[k]:.3f}"
-    assert identical >= len(prompts) // 2
+    assert all(len(set(t)) >= 4 for t in want)
+    got = paged_forced_argmax(model, prompts, want)
+    diffs, bad = forced_agreement(got, want, margins, tie=0.05)
+    assert not bad, f"argmax differs away from a near-tie (prompt, step, oracle top-2 margin): {bad}"
+    assert len(diffs) <= len(prompts) * n_new // 20, diffs
 
 
 def test_fp32_packed_chunked_prefill_matches_per_request_prefill(cuda, native_lib):
