@@ -123,6 +123,7 @@ constexpr int kMaxRanks = BL_MAX_RANKS;
 struct OutTargets {
   void* ptr[kMaxRanks];
   int32_t n;
+  int32_t vec16;  // every ptr 16-byte aligned and the row strides multiples of 16 bytes
 };
 
 inline OutTargets one_target(void* p) {
@@ -132,6 +133,14 @@ inline OutTargets one_target(void* p) {
   return t;
 }
 
+// Marks the targets for 16-byte stores when every buffer and the batch / head
+// strides (in elements of `elem_bytes`) keep 16-byte alignment.
+inline void set_vec16(OutTargets& t, int64_t stride_b, int64_t stride_h, int elem_bytes) {
+  bool ok = elem_bytes > 0 && (stride_b * elem_bytes) % 16 == 0 && (stride_h * elem_bytes) % 16 == 0;
+  for (int p = 0; p < t.n; ++p) ok = ok && ((uintptr_t)t.ptr[p] % 16 == 0);
+  t.vec16 = ok ? 1 : 0;
+}
+
 // The loop is unrolled over the fixed bound so every ptr[] index is static
 // (no local-memory copy of the kernel parameter).
 template <typename T>
@@ -139,6 +148,16 @@ __device__ __forceinline__ void store_targets(const OutTargets& o, int64_t off, 
 #pragma unroll
   for (int p = 0; p < kMaxRanks; ++p)
     if (p < o.n) reinterpret_cast<T*>(o.ptr[p])[off] = v;
+}
+
+// 16 bytes (eight 16-bit elements starting at element `off`) to every
+// target; the caller checked OutTargets::vec16.  Peer targets receive one
+// 16-byte store per eight elements instead of eight 2-byte stores.
+template <typename T>
+__device__ __forceinline__ void store_targets_x16b(const OutTargets& o, int64_t off, uint4 v) {
+#pragma unroll
+  for (int p = 0; p < kMaxRanks; ++p)
+    if (p < o.n) *reinterpret_cast<uint4*>(reinterpret_cast<T*>(o.ptr[p]) + off) = v;
 }
 
 // Release / acquire at system scope, for flags another GPU reads or writes.

@@ -477,6 +477,41 @@ __global__ void __launch_bounds__(kThreadsTC) decode_tc_kernel(const TCArgs a,
     }
     named_barrier_sync(1, kNW * 32);
     const int ctid = threadIdx.x;  // 0 .. kNW*32-1
+    if (nch <= 1 && a.out.vec16) {
+      // a one-chunk row's output: eight consecutive dims per thread, one
+      // 16-byte store per target
+      for (int e = ctid; e < a.g * (kD / 8); e += kNW * 32) {
+        const int hd = e / (kD / 8);
+        const int d0 = (e - hd * (kD / 8)) * 8;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kNW; ++w) M = fmaxf(M, comb_ml[(w * 8 + hd) * 2]);
+        float L = 0.f, O[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int w = 0; w < kNW; ++w) {
+          const float mw = comb_ml[(w * 8 + hd) * 2];
+          const float f = (mw == -INFINITY) ? 0.f : fast_exp2(mw - M);
+          L += f * comb_ml[(w * 8 + hd) * 2 + 1];
+          const float4* src = reinterpret_cast<const float4*>(comb_o + (w * a.g + hd) * kD + d0);
+          const float4 u = src[0], v = src[1];
+          O[0] += f * u.x, O[1] += f * u.y, O[2] += f * u.z, O[3] += f * u.w;
+          O[4] += f * v.x, O[5] += f * v.y, O[6] += f * v.z, O[7] += f * v.w;
+        }
+        // the same arithmetic as the element-wise path below (O / L), so the
+        // result does not depend on which store path runs
+        float r[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) r[i] = (L > 0.f) ? O[i] / L : 0.f;
+        uint4 pk;
+        pk.x = pack2<T>(r[0], r[1]);
+        pk.y = pack2<T>(r[2], r[3]);
+        pk.z = pack2<T>(r[4], r[5]);
+        pk.w = pack2<T>(r[6], r[7]);
+        store_targets_x16b<T>(a.out, (int64_t)b * a.o_sb + (int64_t)(h * a.g + hd) * a.o_sh + d0, pk);
+      }
+      named_barrier_sync(1, kNW * 32);
+      continue;
+    }
     for (int e = ctid; e < a.g * kD; e += kNW * 32) {
       const int hd = e / kD;
       const int d = e - hd * kD;
@@ -536,17 +571,26 @@ __global__ void __launch_bounds__(256) decode_reduce_kernel(const ReduceArgs a) 
   if (base < 0 || base + nch > a.max_units) return;  // plan overflow, flagged by the plan kernel
   float M = -INFINITY;
   for (int c = 0; c < nch; ++c) M = fmaxf(M, a.ws_lse[(base + c) * a.hq + hq]);
-  for (int d = threadIdx.x; d < a.d; d += blockDim.x) {
-    float num = 0.f, den = 0.f;
-    for (int c = 0; c < nch; ++c) {
-      const float lse = a.ws_lse[(base + c) * a.hq + hq];
-      const float w = (lse == -INFINITY) ? 0.f : fast_exp2(lse - M);
-      num += w * a.ws_o[((base + c) * a.hq + hq) * a.d + d];
-      den += w;
-    }
-    store_targets<T>(a.out, (int64_t)b * a.o_sb + (int64_t)hq * a.o_sh + d,
-                     from_f32<T>(den > 0.f ? num / den : 0.f));
+  // blockDim.x == a.d: one output element per thread
+  __shared__ __align__(16) T s_out[kD];
+  const int d = threadIdx.x;
+  float num = 0.f, den = 0.f;
+  for (int c = 0; c < nch; ++c) {
+    const float lse = a.ws_lse[(base + c) * a.hq + hq];
+    const float w = (lse == -INFINITY) ? 0.f : fast_exp2(lse - M);
+    num += w * a.ws_o[((base + c) * a.hq + hq) * a.d + d];
+    den += w;
   }
+  const T val = from_f32<T>(den > 0.f ? num / den : 0.f);
+  const int64_t row = (int64_t)b * a.o_sb + (int64_t)hq * a.o_sh;
+  if (!a.out.vec16) {
+    store_targets<T>(a.out, row + d, val);
+    return;
+  }
+  // the row leaves as 16-byte stores (one per eight elements and target)
+  s_out[d] = val;
+  __syncthreads();
+  if (d < kD / 8) store_targets_x16b<T>(a.out, row + d * 8, reinterpret_cast<const uint4*>(s_out)[d]);
 }
 
 // ---------------------------------------------------------------------------
@@ -876,15 +920,18 @@ bool is_tc(const bl_decode_args& a) {
 namespace bl {
 namespace {
 
-// The attention kernel of a checked call, storing to `ot`.
-int decode_attention(const bl_decode_args& a, const OutTargets& ot, cudaStream_t s) {
+// The attention kernel of a checked call, storing to `targets`.
+int decode_attention(const bl_decode_args& a, const OutTargets& targets, cudaStream_t s) {
   if (is_tc(a)) {
     WsLayout w;
     const int rc = check_tc(a, w);
     if (rc) return rc;
+    OutTargets ot = targets;
+    set_vec16(ot, a.out_stride_b, a.out_stride_h, elem_size(a.kv.dtype));
     if (a.kv.dtype == BL_BF16) return launch_tc_attention<__nv_bfloat16>(a, ot, w, s);
     return launch_tc_attention<__half>(a, ot, w, s);
   }
+  const OutTargets& ot = targets;
   switch (a.kv.dtype) {
     case BL_F32: return launch_simt<float>(a, ot, s);
     case BL_F16: return launch_simt<__half>(a, ot, s);
@@ -892,12 +939,14 @@ int decode_attention(const bl_decode_args& a, const OutTargets& ot, cudaStream_t
   }
 }
 
-// The split-K reduce of a checked call, storing to `ot`.
-int decode_reduce(const bl_decode_args& a, const OutTargets& ot, cudaStream_t s) {
+// The split-K reduce of a checked call, storing to `targets`.
+int decode_reduce(const bl_decode_args& a, const OutTargets& targets, cudaStream_t s) {
   if (!is_tc(a)) return BL_OK;  // the SIMT path never splits
   WsLayout w;
   const int rc = check_tc(a, w);
   if (rc) return rc;
+  OutTargets ot = targets;
+  set_vec16(ot, a.out_stride_b, a.out_stride_h, elem_size(a.kv.dtype));
   if (a.kv.dtype == BL_BF16) return launch_tc_reduce<__nv_bfloat16>(a, ot, w, s);
   return launch_tc_reduce<__half>(a, ot, w, s);
 }

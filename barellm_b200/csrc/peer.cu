@@ -78,14 +78,24 @@ PFN_cuMemGetAddressRange_v3020 get_range_fn() {
   return fn;
 }
 
-// addresses returned by bl_ipc_import and the mapping base each belongs to
+// CUDA IPC lets a process open a given allocation only once, and the
+// exporter hands out the handle of the whole allocation (a caching-allocator
+// segment can hold the regions of several objects).  So mappings are shared:
+// one entry per distinct handle with a count of the addresses handed out from
+// it, and the allocation is unmapped when the last of them is closed.
 struct Mapping {
-  void* user;
+  unsigned char handle[sizeof(cudaIpcMemHandle_t)];
   void* base;
+  int refs;
 };
+struct UserAddr {
+  void* user;
+  int mapping;  // index into g_maps
+};
+constexpr int kMaxMappings = 256;
 std::mutex g_map_mu;
-Mapping g_maps[256];
-
+Mapping g_maps[kMaxMappings];
+UserAddr g_users[kMaxMappings];
 }  // namespace
 
 int check_head_gather(const bl_head_gather& g, const char* who) {
@@ -151,41 +161,70 @@ extern "C" int bl_ipc_import(const bl_ipc_handle* handle, void** ptr) {
   BL_CHECK_ARG(handle != nullptr && ptr != nullptr, "bl_ipc_import: null argument");
   cudaIpcMemHandle_t h;
   std::memcpy(&h, handle->bytes, sizeof(h));
-  void* base = nullptr;
-  const cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
-  if (e != cudaSuccess) {
-    set_error("bl_ipc_import: cudaIpcOpenMemHandle failed: %s", cudaGetErrorString(e));
-    return BL_ERR_LAUNCH;
-  }
-  void* user = (char*)base + handle->offset;
   std::lock_guard<std::mutex> lk(g_map_mu);
-  for (auto& m : g_maps)
-    if (m.user == nullptr) {
-      m.user = user;
-      m.base = base;
-      *ptr = user;
-      return BL_OK;
+  int slot = -1;
+  for (int u = 0; u < kMaxMappings; ++u)
+    if (g_users[u].user == nullptr) {
+      slot = u;
+      break;
     }
-  cudaIpcCloseMemHandle(base);
-  set_error("bl_ipc_import: more than 256 mappings are open");
-  return BL_ERR_CAPACITY;
+  if (slot < 0) {
+    set_error("bl_ipc_import: more than %d imported addresses are open", kMaxMappings);
+    return BL_ERR_CAPACITY;
+  }
+  int m = -1;
+  for (int i = 0; i < kMaxMappings; ++i)
+    if (g_maps[i].refs > 0 && std::memcmp(g_maps[i].handle, &h, sizeof(h)) == 0) {
+      m = i;  // this allocation is mapped already: share the mapping
+      break;
+    }
+  if (m < 0) {
+    for (int i = 0; i < kMaxMappings; ++i)
+      if (g_maps[i].refs == 0) {
+        m = i;
+        break;
+      }
+    // at most kMaxMappings user addresses exist, each holding one mapping, so a free entry remains
+    void* base = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      set_error("bl_ipc_import: cudaIpcOpenMemHandle failed: %s", cudaGetErrorString(e));
+      return BL_ERR_LAUNCH;
+    }
+    std::memcpy(g_maps[m].handle, &h, sizeof(h));
+    g_maps[m].base = base;
+    g_maps[m].refs = 0;
+  }
+  g_maps[m].refs += 1;
+  void* user = (char*)g_maps[m].base + handle->offset;
+  g_users[slot].user = user;
+  g_users[slot].mapping = m;
+  *ptr = user;
+  return BL_OK;
 }
 
 extern "C" int bl_ipc_close(void* ptr) {
   BL_CHECK_ARG(ptr != nullptr, "bl_ipc_close: null pointer");
-  void* base = nullptr;
+  void* unmap = nullptr;
   {
     std::lock_guard<std::mutex> lk(g_map_mu);
-    for (auto& m : g_maps)
-      if (m.user == ptr) {
-        base = m.base;
-        m.user = nullptr;
-        m.base = nullptr;
+    int slot = -1;
+    for (int u = 0; u < kMaxMappings; ++u)
+      if (g_users[u].user == ptr) {
+        slot = u;
         break;
       }
+    BL_CHECK_ARG(slot >= 0, "bl_ipc_close: address was not returned by bl_ipc_import (or is closed)");
+    Mapping& m = g_maps[g_users[slot].mapping];
+    g_users[slot].user = nullptr;
+    if (--m.refs == 0) {
+      unmap = m.base;
+      m.base = nullptr;
+      std::memset(m.handle, 0, sizeof(m.handle));
+    }
   }
-  BL_CHECK_ARG(base != nullptr, "bl_ipc_close: address was not returned by bl_ipc_import");
-  const cudaError_t e = cudaIpcCloseMemHandle(base);
+  if (unmap == nullptr) return BL_OK;  // other addresses still use this mapping
+  const cudaError_t e = cudaIpcCloseMemHandle(unmap);
   if (e != cudaSuccess) {
     set_error("bl_ipc_close: cudaIpcCloseMemHandle failed: %s", cudaGetErrorString(e));
     return BL_ERR_LAUNCH;

@@ -63,6 +63,17 @@ class HeadShardedDecode:
     ``[batch, Hq, D]`` output.  The gathered buffers alternate (``buffers``
     of them), so a returned tensor stays valid until ``buffers - 1`` further
     calls have been made; every rank must make the same sequence of calls.
+
+    Errors on the device (a bad block id, a barrier wait that timed out) go
+    to a device error word: the caller's ``err`` when given, else one this
+    object owns.  :meth:`check_device_errors` reads it (a device sync) and
+    raises; :meth:`close` checks it as well.  A barrier time-out (a peer that
+    did not finish the call within ``timeout_s``) is fatal to the call: its
+    gathered output is undefined, and since this rank's epoch has moved on,
+    the two-buffer guarantee no longer holds either -- close the object on
+    every rank and build a new one (a collective) before decoding again.
+    ``timeout_s`` bounds how far one rank's host may fall behind the others
+    (first-call set-up, a collection pause); it is 10 s by default.
     """
 
     def __init__(
@@ -76,7 +87,7 @@ class HeadShardedDecode:
         *,
         group=None,
         buffers: int = 2,
-        timeout_s: float = 2.0,
+        timeout_s: float = 10.0,
     ):
         import torch.distributed as dist
 
@@ -120,6 +131,7 @@ class HeadShardedDecode:
         g.head_offset = self.q_heads[0]
         g.timeout_ns = int(timeout_s * 1e9)
         self._g = g
+        self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._closed = False
 
     def decode(
@@ -143,9 +155,12 @@ class HeadShardedDecode:
 
         ``q``: ``[batch, Hq/W, D]`` (or ``[batch, Hq/W, 1, D]``), this rank's
         query heads; ``key_cache`` / ``value_cache``: this rank's pool shard
-        ``[L, P, Hkv/W, bs, D]``.  The scale defaults to 1/sqrt(D)."""
+        ``[L, P, Hkv/W, bs, D]``.  The scale defaults to 1/sqrt(D).
+        ``err``: a device int32 error word; None uses this object's own."""
         if self._closed:
             raise RuntimeError("HeadShardedDecode is closed")
+        if err is None:
+            err = self.err
         q0, q1 = self.q_heads
         k = self._next
         out = self.outs[k]
@@ -162,8 +177,18 @@ class HeadShardedDecode:
         self._next = (k + 1) % len(self.outs)
         return out
 
+    def check_device_errors(self) -> None:
+        """Raises RuntimeError if this object's device error word is set
+        (waits for the device).  Errors sent to a caller's ``err`` word are
+        the caller's to check."""
+        word = int(self.err.item())
+        if word:
+            raise RuntimeError(ops.describe_device_error(word) + " in the head-sharded decode "
+                               "(after a barrier time-out the gathered outputs are undefined)")
+
     def close(self) -> None:
-        """Unmaps the other ranks' buffers (a collective: ends at a barrier)."""
+        """Unmaps the other ranks' buffers (a collective: ends at a barrier),
+        then raises if this object's device error word is set."""
         import torch.distributed as dist
 
         if self._closed:
@@ -176,6 +201,7 @@ class HeadShardedDecode:
                 ops.ipc_close(self._bases[r])
                 self._bases[r] = 0
         self._closed = True
+        self.check_device_errors()
 
 
 def gather_heads_collective(out_local: torch.Tensor, group=None) -> torch.Tensor:

@@ -28,6 +28,15 @@ def _check(cond: bool, message: str) -> None:
         raise ValueError(message)
 
 
+def describe_device_error(word: int) -> str:
+    """Names the BL_DEVERR_* bits of a device error word."""
+    names = [(nat.BL_DEVERR_BLOCK_ID, "block id outside the pool"), (nat.BL_DEVERR_TABLE, "block table overrun"),
+             (nat.BL_DEVERR_TIMEOUT, "bounded wait timed out"),
+             (nat.BL_DEVERR_WORKSPACE, "split-K workspace holds no matching plan")]
+    found = [text for bit, text in names if word & bit]
+    return f"device error word {word:#x} ({'; '.join(found) or 'unknown bits'})"
+
+
 def _raise_rc(rc: int) -> None:
     if rc == nat.BL_OK:
         return

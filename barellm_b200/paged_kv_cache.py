@@ -200,13 +200,15 @@ class PagedKVCache:
         return self._err
 
     def check_device_errors(self) -> None:
-        """Synchronises and raises if any kernel flagged a bad block id."""
+        """Synchronises and raises if any kernel flagged an error (a bad block
+        id, a table overrun, a timed-out wait) in this pool's error word; the
+        word is cleared first."""
         if self._err is None:
             return
         code = int(self._err.item())
         if code:
             self._err.zero_()
-            raise RuntimeError(f"paged-KV kernel reported device error bits {code:#x}")
+            raise RuntimeError("paged-KV kernel reported " + ops.describe_device_error(code))
 
     def register_request(self, request_id: str, blocks: list[KVCacheBlock]) -> None:
         pages = self.request_pages.get(request_id)

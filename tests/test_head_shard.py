@@ -171,6 +171,25 @@ def test_world1_equals_decode_bit_for_bit(cuda, native_lib, name, dtype):
     h.close()
 
 
+@pytest.mark.gpu
+def test_own_error_word_reports_a_bad_block_id(cuda, native_lib):
+    """Without a caller error word the object's own word receives the
+    kernels' error bits; check_device_errors (and close) raise on it."""
+    st = _state("decode_qwen06b_b4", torch.bfloat16, cuda)
+    c = st.case
+    bt = st.bt.clone()
+    bt[0, 0] = c.num_blocks + 5  # flagged by the kernel, the access skipped
+    h = hs.HeadShardedDecode(c.batch, c.num_q_heads, c.num_kv_heads, c.head_dim, torch.bfloat16, cuda)
+    h.decode(st.q, st.k_cache, st.v_cache, 0, st.bt, st.seq_lens, max(st.seq_lens_list))
+    h.check_device_errors()  # a clean call leaves the word clear
+    h.decode(st.q, st.k_cache, st.v_cache, 0, bt, st.seq_lens, max(st.seq_lens_list))
+    with pytest.raises(RuntimeError, match="block id outside the pool"):
+        h.check_device_errors()
+    with pytest.raises(RuntimeError, match="block id outside the pool"):
+        h.close()
+    assert h._closed
+
+
 class _EmulatedRanks:
     """Two ranks' regions (signal pad, epoch, gathered buffer) on one device."""
 
@@ -306,3 +325,58 @@ def test_two_gpus_fused_gather_equals_unsharded_decode():
         assert err == 0, res
         for fused_ok, coll_ok, diff in res:
             assert fused_ok and coll_ok, (r, res)
+
+
+def _two_objects_worker(rank: int, world: int, port: int, out) -> None:
+    """Two HeadShardedDecode objects alive at once in each process (their
+    regions may share one allocation, so their peer mappings are shared);
+    closing the first must leave the second's mappings intact."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    first = second = None
+    try:
+        st = _state("decode_qwen8b_b3", torch.bfloat16, dev)
+        c = st.case
+        k, v, _, (q0, q1) = _shard(st, world, rank)
+        first = hs.HeadShardedDecode(c.batch, c.num_q_heads, c.num_kv_heads, c.head_dim, torch.bfloat16, dev)
+        second = hs.HeadShardedDecode(c.batch, c.num_q_heads, c.num_kv_heads, c.head_dim, torch.bfloat16, dev)
+        ref = ops.paged_decode(st.q, st.k_cache, st.v_cache, 0, st.bt, st.seq_lens, max(st.seq_lens_list))
+        a = first.decode(st.q[:, q0:q1], k, v, 0, st.bt, st.seq_lens, max(st.seq_lens_list)).clone()
+        first.close()
+        res = [bool(torch.equal(a, ref))]
+        for _ in range(3):
+            b = second.decode(st.q[:, q0:q1], k, v, 0, st.bt, st.seq_lens, max(st.seq_lens_list))
+            torch.cuda.synchronize()
+            res.append(bool(torch.equal(b, ref)))
+        second.check_device_errors()
+        out.put((rank, res, 0))
+    except Exception as e:  # noqa: BLE001 - reported to the parent
+        out.put((rank, repr(e), -1))
+    finally:
+        for h in (first, second):
+            if h is not None and not h._closed:
+                h.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_two_gpus_two_objects_share_peer_mappings():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world = 2
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_two_objects_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict((r, (res, err)) for r, res, err in (q.get(timeout=300) for _ in range(world)))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for r in range(world):
+        res, err = results[r]
+        assert err == 0 and all(res), (r, res)
