@@ -88,12 +88,44 @@ bool make_tmap_2d_16bit(CUtensorMap* map, const void* base, uint64_t row_elems, 
   return true;
 }
 
+// Paged pools viewed page by page: x = 64 elements (one 128-byte half of a
+// 256-byte token row), y = 8 token rows (256 B apart), z = the row's two
+// halves (128 B apart), w = groups of 8 rows (2 KB apart).  A box of
+// {64, 8, 2, 2} is one whole 16-token page (4 KB), landing in shared memory as
+// [8-row group][half][8 rows][128 B]: each 1 KB block is one 128-byte-swizzle
+// atom, so a tile of pages is a K-major (or MN-major) tcgen05 operand with an
+// 8-row group stride of 2 KB and the two halves 1 KB apart.
+bool make_tmap_pages_16bit(CUtensorMap* map, const void* base, uint64_t rows, bool bf16) {
+  auto fn = get_encode_fn();
+  if (!fn) {
+    set_error("cuTensorMapEncodeTiled is unavailable from the driver");
+    return false;
+  }
+  if (rows % 8 != 0) {
+    set_error("page tensor map: %llu pool rows is not a multiple of 8", (unsigned long long)rows);
+    return false;
+  }
+  cuuint64_t dims[4] = {64, 8, 2, rows / 8};
+  cuuint64_t strides[3] = {256, 128, 2048};
+  cuuint32_t box[4] = {64, 8, 2, 2};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled (page map) failed with CUresult %d", (int)r);
+    return false;
+  }
+  return true;
+}
+
 namespace {
 struct TmapEntry {
   const void* ptr;
   uint64_t rows;
   int dtype;
   int device;
+  int kind;  // 0: rows (64 x 16 boxes), 1: whole pages
   CUtensorMap map;
 };
 std::mutex g_tmap_mu;
@@ -101,17 +133,19 @@ TmapEntry g_tmaps[32];
 int g_tmap_next = 0;
 }  // namespace
 
-bool get_pool_tmap(const void* pool, uint64_t rows, int dtype, CUtensorMap* out) {
+static bool get_cached_tmap(const void* pool, uint64_t rows, int dtype, int kind, CUtensorMap* out) {
   int dev = 0;
   cudaGetDevice(&dev);
   std::lock_guard<std::mutex> lk(g_tmap_mu);
   for (auto& e : g_tmaps)
-    if (e.ptr == pool && e.rows == rows && e.dtype == dtype && e.device == dev) {
+    if (e.ptr == pool && e.rows == rows && e.dtype == dtype && e.device == dev && e.kind == kind) {
       *out = e.map;
       return true;
     }
   TmapEntry& e = g_tmaps[g_tmap_next];
-  if (!make_tmap_2d_16bit(&e.map, pool, 128, rows, 64, 16, dtype == BL_BF16)) {
+  const bool ok = kind == 0 ? make_tmap_2d_16bit(&e.map, pool, 128, rows, 64, 16, dtype == BL_BF16)
+                            : make_tmap_pages_16bit(&e.map, pool, rows, dtype == BL_BF16);
+  if (!ok) {
     e.ptr = nullptr;
     return false;
   }
@@ -119,9 +153,18 @@ bool get_pool_tmap(const void* pool, uint64_t rows, int dtype, CUtensorMap* out)
   e.rows = rows;
   e.dtype = dtype;
   e.device = dev;
+  e.kind = kind;
   g_tmap_next = (g_tmap_next + 1) % 32;
   *out = e.map;
   return true;
+}
+
+bool get_pool_tmap(const void* pool, uint64_t rows, int dtype, CUtensorMap* out) {
+  return get_cached_tmap(pool, rows, dtype, 0, out);
+}
+
+bool get_pool_page_tmap(const void* pool, uint64_t rows, int dtype, CUtensorMap* out) {
+  return get_cached_tmap(pool, rows, dtype, 1, out);
 }
 
 }  // namespace bl

@@ -246,6 +246,16 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// 4-D tiled TMA load (coordinates x, y, z, w), completion counted on `bar`.
+__device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int32_t x,
+                                            int32_t y, int32_t z, int32_t w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+}
+
 // Same, with an L2 cache-policy hint (evict-first for streamed K/V pages).
 __device__ __forceinline__ void tma_load_2d_hint(void* smem_dst, const CUtensorMap* map,
                                                  uint64_t* bar, int32_t x, int32_t y,
@@ -506,6 +516,11 @@ bool make_tmap_2d_16bit(CUtensorMap* map, const void* base, uint64_t row_elems, 
 // Cached tensor map over a K or V pool viewed as `rows` rows of 128 16-bit
 // elements, box 64 x 16, 128-byte swizzle (one 16-token page half per box).
 bool get_pool_tmap(const void* pool, uint64_t rows, int dtype, CUtensorMap* out);
+
+// Cached tensor map over a K or V pool that copies one whole 16-token page
+// (4 KB) per box, laid out in shared memory as [8-row group][half][8 rows]
+// [128 B] with the 128-byte swizzle (make_tmap_pages_16bit in abi.cu).
+bool get_pool_page_tmap(const void* pool, uint64_t rows, int dtype, CUtensorMap* out);
 
 // Validates a bl_head_gather descriptor (host side).
 int check_head_gather(const bl_head_gather& g, const char* who);

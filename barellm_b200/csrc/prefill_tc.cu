@@ -2,38 +2,43 @@
 // tensor memory), bf16 / fp16, head_dim 128, block_size 16, GQA group G in
 // {1, 2, 4, 8}.
 //
-// A CTA owns one 128-row MMA tile of score rows = (128 / G) query tokens x
-// the G query heads that share one KV head (head-major rows), and walks the
-// keys in tiles of 128 (8 pages).  Tensor memory (512 columns) holds two S
-// buffers, the O accumulator and two P buffers:
-//   S0 0..127, S1 128..255, O 256..383, P0 384..447, P1 448..511,
-// so no step waits for the one before it to release its columns: S(t+1) is
-// computed into the other S buffer while the softmax of tile t runs, and
-// P(t) goes to its own columns, where the P V MMA reads it as its A operand.
-// Warp roles (8 warps, 1 CTA per SM):
-//   warp 0      K producer (one lane): the 8 pages of key tile t as 2-D TMA
-//               boxes (64 x 16, 128-byte swizzle) into a 3-stage K ring; a
-//               page past the row's last page is read at an out-of-range row
-//               coordinate, which TMA fills with zeros.
-//   warp 1      V producer: the V pages of tile t into a 3-stage V ring, as
-//               the same TMA boxes (lane 0), except the page holding the
+// A CTA owns 256 score rows = (256 / G) query tokens x the G query heads that
+// share one KV head, as two 128-row tiles A and B (head-major rows, so for
+// G >= 2 both tiles cover the same tokens and need the same keys).  Every K/V
+// page is fetched once for 256 rows, which halves the K/V bytes per flop of a
+// 128-row tile; keys are consumed in tiles of 128 (8 pages).  Warp roles (12 warps):
+//   warp 0      K producer: the 8 pages of key tile t, one TMA box per whole
+//               4 KB page (a 4-D view of the pool, 128-byte swizzle; lanes
+//               0..7 one page each), into a 2-stage K ring; a page past the
+//               row's last page is read at an out-of-range coordinate, which
+//               TMA fills with zeros.  A page lands as [8-row group][half]
+//               [8 rows][128 B], so a tile is an MMA operand whose 8-key groups
+//               are 2 KB apart and whose two 64-element halves are 1 KB apart.
+//   warp 1      V producer: the V pages of tile t-1 into a 3-stage V ring, as
+//               the same TMA boxes (lanes 0..7), except the page holding the
 //               row's last key when the row ends inside it: the 32 lanes copy
 //               it with 16-byte cp.async, zero-filling the slots past the row
 //               length (src-size 0), so stale pool bytes never reach P V.
 //               TMA bytes and the lanes' cp.async arrivals complete the
-//               stage's mbarrier together.
-//   warp 2      TMEM owner and, on one lane, the MMA issuer: per key tile t it
-//               issues S(t) = Q K_t^T into S[t%2] (once the softmax has read
-//               S(t-2) out of it), then O += P(t-1) V_{t-1} (once P(t-1) is
-//               written), so the tensor pipe computes S(t+1) and P V while
-//               the softmax of tile t runs.  (Warp 3 has no role.)
-//   warps 4..7  softmax, one thread per score row (= TMEM lane): S row read
-//               from TMEM once into registers (bottom-right causal mask, row
-//               max in log2 units), exponentiated and written as packed
-//               bf16/fp16 P into P[t%2] (after the P V that last read that
-//               buffer completed); a lazy rescale touches O only when the
-//               running max grows by more than 2^8 (after the previous P V
-//               has landed in O).  Epilogue: O / l from TMEM to global.
+//               stage's mbarrier together.  (Warp 2 has no role.)
+//               Both producer warps hold the row's block-table entries 32 at
+//               a time across their lanes and read the next 32 while using
+//               the current ones: a dependent table read per page (eight per
+//               tile, one after another) had held the producers to ~3.5 k
+//               cycles per tile.
+//   warp 3      TMEM owner (512 columns: S_A 0..127, S_B 128..255, O_A 256..383,
+//               O_B 384..511) and, on one lane, the MMA issuer.  Per key tile t
+//               it issues O_A += P_A V_{t-1}, S_A = Q_A K_t^T, O_B += P_B V_{t-1},
+//               S_B = Q_B K_t^T, so one tile's softmax runs while the tensor
+//               pipe works on the other tile.  S_X is rewritten only after the
+//               P V that read P_X (stored in S_X's columns) has completed.
+//   warps 4..7  softmax of tile A, warps 8..11 of tile B: one thread per score
+//               row (= TMEM lane).  The S row is read from TMEM once into
+//               registers (bottom-right causal mask, row max in log2 units),
+//               exponentiated and written back as packed bf16/fp16 P over the
+//               first 64 S columns, where the P V MMA reads it as its A
+//               operand; a lazy rescale touches O only when the running max
+//               grows by more than 2^8.  Epilogue: O / l from TMEM to global.
 // Every mbarrier wait is bounded; on a time-out the CTA records
 // BL_DEVERR_TIMEOUT, drains what it issued and frees its TMEM.
 // Roofline: tensor.  Algorithmic flops per request: 4 * Hq * D * (C*P + C(C+1)/2).
@@ -48,26 +53,26 @@ constexpr int kD = 128;
 constexpr int kBS = 16;
 constexpr int kKT = 128;                 // keys per tile
 constexpr int kPPT = kKT / kBS;          // 8 pages per tile
-constexpr int kRows = 128;               // score rows per CTA (one MMA tile, M)
-constexpr int kKStages = 3;              // K: 3 x 32 KB
-constexpr int kVStages = 3;              // V: 3 x 32 KB
-constexpr int kKWarp = 0;
-constexpr int kVWarp = 1;
-constexpr int kMmaWarp = 2;
-constexpr int kSoftmaxWarp0 = 4;         // warps 4..7: TMEM lane quadrants 0..3
-constexpr int kThreads = 256;
-constexpr int kHalf = 128 * 128;         // 16 KB: 128 rows x 128 B (64 elements of D or K)
+constexpr int kTileRows = 128;           // rows per MMA tile (M)
+constexpr int kRows = 2 * kTileRows;     // score rows per CTA
+constexpr int kKStages = 2;             // K: 2 x 32 KB (S of tile t+1 is issued after P V of t-1)
+constexpr int kVStages = 3;             // V: 3 x 32 KB (V is read last, by P V)
+constexpr int kMmaWarp = 3;
+constexpr int kSoftmaxWarp0 = 4;
+constexpr int kThreads = 384;            // 3 producer warps, MMA warp, 2 x 4 softmax warps
+constexpr int kHalf = 128 * 128;         // 16 KB: a Q tile's 128 rows x 128 B (64 elements of D)
 constexpr int kTile = 2 * kHalf;         // 32 KB
-constexpr int kOffQ = 0;                         // Q: one 32 KB tile
-constexpr int kOffK = kTile;                     // + s * kTile
+constexpr int kPage = kBS * kD * 2;      // 4 KB: one page in a K / V stage
+constexpr int kGroup = 2048;             // 8 key rows (both halves) in a K / V stage
+constexpr int kOffQ = 0;                        // + X * kTile
+constexpr int kOffK = 2 * kTile;                // + s * kTile
 constexpr int kOffV = kOffK + kKStages * kTile;  // + s * kTile
 constexpr int kSmemData = kOffV + kVStages * kTile;  // 224 KB
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS = 0;                    // + (t % 2) * 128
-constexpr uint32_t kColO = 256;
-constexpr uint32_t kColP = 384;                  // + (t % 2) * 64
+constexpr uint32_t kColS = 0;                   // + X * 128 (P_X aliases the first 64 columns)
+constexpr uint32_t kColO = 256;                 // + X * 128
 constexpr float kLog2e = 1.4426950408889634f;
-constexpr float kRescaleThreshold = 8.0f;        // log2 units
+constexpr float kRescaleThreshold = 8.0f;       // log2 units
 
 struct Args {
   const void* q;
@@ -92,7 +97,7 @@ struct Args {
 
 struct Shared {
   uint64_t full_k[kKStages], full_v[kVStages], empty_k[kKStages], empty_v[kVStages];
-  uint64_t s_full[2], s_free[2], p_full[2], pv_done[2], q_full, mma_done;
+  uint64_t s_full[2], p_full[2], pv_done[2], q_full, mma_done;
   uint32_t tmem_base;
   int abort;
 };
@@ -146,8 +151,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(&sh->s_full[x], 1);
-      mbar_init(&sh->s_free[x], kRows);  // one arrival per softmax thread
-      mbar_init(&sh->p_full[x], kRows);
+      mbar_init(&sh->p_full[x], kTileRows);
       mbar_init(&sh->pv_done[x], 1);
     }
     mbar_init(&sh->q_full, kRows);
@@ -161,47 +165,64 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = sh->tmem_base;
 
-  if (warp == kKWarp || warp == kVWarp) {
+  if (warp < kMmaWarp) {
     // ------------------------------ producers ------------------------------
     const int64_t brow = a.row_ids ? (int64_t)a.row_ids[b] : b;
     const int32_t* bt = a.block_tables + brow * a.bt_stride;
-    if (warp == kKWarp) {
-      // K: one TMA per page half (64 x 16 box, 128-byte swizzle); pages past
-      // the row's last page come from an out-of-range row, which TMA fills
+    // The row's block-table entries reach each producer warp 32 at a time
+    // (four key tiles), lane i holding page 32k + i, and the next 32 are read
+    // while the current ones are in use: a producer never waits on a
+    // dependent table read per page (eight of them in a row cost more than a
+    // whole tile's MMAs).
+    auto bt_at = [&](int lb) -> int32_t { return lb < npages ? bt[lb] : -1; };
+    int32_t win_cur = bt_at(lane), win_nxt = bt_at(32 + lane);
+    auto advance = [&](int t) {
+      if (t > 0 && (t & 3) == 0) {
+        win_cur = win_nxt;
+        win_nxt = bt_at((t + 4) * kPPT + lane);
+      }
+    };
+    // the pool coordinate of page lb (held by this lane), or out of range
+    auto page_w = [&](int lb, int32_t phys, bool flag) -> int32_t {
+      if (lb >= npages) return a.rows_total / 8;  // past the row: zeros
+      if (phys < 0 || phys >= a.num_blocks) {
+        if (flag) raise_dev(a.err, BL_DEVERR_BLOCK_ID);
+        return a.rows_total / 8;
+      }
+      return (int32_t)((a.layer_row0 + ((int64_t)phys * a.hkv + h) * kBS) / 8);
+    };
+    if (warp == 0) {
+      // K: one TMA box per page, lanes 0..7 one page each; pages past the
+      // row's last page come from an out-of-range coordinate, which TMA fills
       // with zeros (stale rows inside the last page are masked out of S).
       if (lane == 0) {
         if (table_short) raise_dev(a.err, BL_DEVERR_TABLE);
         prefetch_tensormap(&kmap);
-        int issued = 0;
-        for (int t = 0; t < ntiles; ++t) {
-          const int s = t % kKStages;
-          if (!wait_or_abort(&sh->empty_k[s], ((t / kKStages) & 1) ^ 1, sh, a.err)) break;
-          unsigned char* dst = smem + kOffK + s * kTile;
-          mbar_arrive_expect_tx(&sh->full_k[s], kTile);
-#pragma unroll 1
-          for (int p = 0; p < kPPT; ++p) {
-            const int lb = t * kPPT + p;
-            int32_t y = a.rows_total;
-            if (lb < npages) {
-              const int64_t phys = bt[lb];
-              if (phys < 0 || phys >= a.num_blocks)
-                raise_dev(a.err, BL_DEVERR_BLOCK_ID);
-              else
-                y = (int32_t)(a.layer_row0 + (phys * a.hkv + h) * kBS);
-            }
-            tma_load_2d(dst + p * kBS * 128, &kmap, &sh->full_k[s], 0, y);
-            tma_load_2d(dst + kHalf + p * kBS * 128, &kmap, &sh->full_k[s], 64, y);
-          }
-          ++issued;
+      }
+      int issued = 0;
+      for (int t = 0; t < ntiles; ++t) {
+        advance(t);
+        const int s = t % kKStages;
+        if (!__all_sync(0xffffffffu, wait_or_abort(&sh->empty_k[s], ((t / kKStages) & 1) ^ 1, sh, a.err))) break;
+        const int32_t phys = __shfl_sync(0xffffffffu, win_cur, (t & 3) * kPPT + (lane & (kPPT - 1)));
+        unsigned char* dst = smem + kOffK + s * kTile;
+        if (lane == 0) mbar_arrive_expect_tx(&sh->full_k[s], kTile);
+        __syncwarp();
+        if (lane < kPPT) {
+          const int32_t w = page_w(t * kPPT + lane, phys, true);
+          tma_load_4d(dst + lane * kPage, &kmap, &sh->full_k[s], 0, 0, 0, w);
         }
-        // drain: the K copies in flight land before the CTA can exit
+        ++issued;
+      }
+      // drain: the K copies in flight land before the CTA can exit
+      if (lane == 0) {
         for (int s = 0; s < kKStages && s < issued; ++s) {
           const int last = s + ((issued - 1 - s) / kKStages) * kKStages;
           if (!mbar_wait(&sh->full_k[s], (last / kKStages) & 1)) raise_dev(a.err, BL_DEVERR_TIMEOUT);
         }
       }
-    } else {
-      // V: the tile's pages as 2-D TMA boxes like K (lane 0), except the page
+    } else if (warp == 1) {
+      // V: the tile's pages as TMA boxes like K (lanes 0..7), except the page
       // holding the row's last key when the row ends inside it.  Its slots
       // past the length may hold stale pool bytes (NaN included), which P V
       // would turn into NaN even where P = 0, so the warp copies that page
@@ -212,40 +233,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) prefetch_tensormap(&vmap);
       int issued = 0;
       for (int j = 0; j < ntiles; ++j) {
+        advance(j);
         const int s = j % kVStages;
         if (!__all_sync(0xffffffffu, wait_or_abort(&sh->empty_v[s], ((j / kVStages) & 1) ^ 1, sh, a.err))) break;
         unsigned char* stage = smem + kOffV + s * kTile;
         const int64_t first = (int64_t)j * kPPT;
         const int pp = (part_lb >= first && part_lb < first + kPPT && part_lb < npages) ? (int)(part_lb - first) : -1;
-        if (lane == 0) {
-          mbar_arrive_expect_tx(&sh->full_v[s], (pp >= 0 ? kPPT - 1 : kPPT) * 2 * kBS * 128);
-#pragma unroll 1
-          for (int p = 0; p < kPPT; ++p) {
-            if (p == pp) continue;
-            const int lb = j * kPPT + p;
-            int32_t y = a.rows_total;  // out of range: zeros
-            if (lb < npages) {
-              const int64_t phys = bt[lb];
-              if (phys >= 0 && phys < a.num_blocks) y = (int32_t)(a.layer_row0 + (phys * a.hkv + h) * kBS);
-            }
-            tma_load_2d(stage + p * kBS * 128, &vmap, &sh->full_v[s], 0, y);
-            tma_load_2d(stage + kHalf + p * kBS * 128, &vmap, &sh->full_v[s], 64, y);
-          }
+        const int32_t phys = __shfl_sync(0xffffffffu, win_cur, (j & 3) * kPPT + (lane & (kPPT - 1)));
+        const int32_t ph = __shfl_sync(0xffffffffu, win_cur, (j & 3) * kPPT + (pp >= 0 ? pp : 0));
+        if (lane == 0) mbar_arrive_expect_tx(&sh->full_v[s], (pp >= 0 ? kPPT - 1 : kPPT) * kPage);
+        __syncwarp();
+        if (lane < kPPT && lane != pp) {
+          const int32_t w = page_w((int)first + lane, phys, false);
+          tma_load_4d(stage + lane * kPage, &vmap, &sh->full_v[s], 0, 0, 0, w);
         }
         if (pp >= 0) {
-          // 16 rows x 16 chunks of 16 bytes, eight per lane, in the 128-byte
-          // swizzled layout the TMA boxes produce
+          // 16 rows x 16 chunks of 16 bytes, eight per lane, in the layout the
+          // page boxes produce: [8-row group][half][8 rows][128 B], swizzled
           const int64_t lb = first + pp;
-          const int64_t ph = bt[lb];
           const bool okp = ph >= 0 && ph < a.num_blocks;
 #pragma unroll
           for (int e = lane; e < kBS * 16; e += 32) {
             const int r = e >> 4, cc = e & 15;
             const uint32_t bytes = (okp && lb * kBS + r < len) ? 16u : 0u;
             const uint16_t* src =
-                a.v_pool + ((a.layer_row0 + ((okp ? ph : 0) * a.hkv + h) * kBS + r) * kD + cc * 8);
-            const uint32_t dst =
-                smem_u32(stage + (cc >> 3) * kHalf + (pp * kBS + r) * 128 + (((cc & 7) ^ (r & 7)) << 4));
+                a.v_pool + ((a.layer_row0 + ((okp ? (int64_t)ph : 0) * a.hkv + h) * kBS + r) * kD + cc * 8);
+            const uint32_t dst = smem_u32(stage + pp * kPage + (r >> 3) * kGroup + (cc >> 3) * 1024 + (r & 7) * 128 +
+                                          (((cc & 7) ^ (r & 7)) << 4));
             asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
           }
         }
@@ -265,69 +279,86 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == kMmaWarp) {
     // ------------------------------ MMA issuer ------------------------------
     if (lane == 0) {
-      const uint32_t idesc_s = umma_idesc_f16(kRows, kKT, BF16, false);
-      const uint32_t idesc_o = umma_idesc_f16(kRows, kD, BF16, true);
+      const uint32_t idesc_s = umma_idesc_f16(kTileRows, kKT, BF16, false);
+      const uint32_t idesc_o = umma_idesc_f16(kTileRows, kD, BF16, true);
+      // O_X += P_X V_j (P_X in S_X's TMEM columns)
       // Shared-memory descriptors are built once; an MMA's operand address is
-      // the base descriptor plus its (16-byte unit) offset.
-      const uint64_t dq = umma_desc_sw128(smem_u32(smem + kOffQ), 16, 1024);
-      const uint64_t dk0 = umma_desc_sw128(smem_u32(smem + kOffK), 16, 1024);
-      const uint64_t dv0 = umma_desc_sw128(smem_u32(smem + kOffV), kHalf, 1024);
-      const uint64_t dstage = (uint64_t)(kTile >> 4);  // one stage, in 16-byte units
-      // A stage's copies land through the async proxy (TMA) or, for V's
-      // partial page, through cp.async; after its mbarrier completes, a proxy
-      // fence orders them before the tensor core's reads.
+      // the base descriptor plus its (16-byte unit) offset, so the single
+      // issuing thread spends a few instructions per MMA (a 128 x 128 x 16 step
+      // takes 64 cycles on the tensor pipe, less than rebuilding descriptors).
+      const uint64_t dq0 = umma_desc_sw128(smem_u32(smem + kOffQ), 16, 1024);
+      const uint64_t dq1 = umma_desc_sw128(smem_u32(smem + kOffQ + kTile), 16, 1024);
+      const uint64_t dk0 = umma_desc_sw128(smem_u32(smem + kOffK), 16, kGroup);  // 8-key groups kGroup apart
+      const uint64_t dk_stride = (uint64_t)(kTile >> 4);  // one K stage, in 16-byte units
+      const uint64_t dv0 = umma_desc_sw128(smem_u32(smem + kOffV), 1024, kGroup);  // MN-major: halves 1 KB apart
+      // O_X += P_X V_j (P_X in S_X's TMEM columns)
+      auto pv = [&](int x, int j) -> bool {
+        if (!wait_or_abort(&sh->p_full[x], j & 1, sh, a.err)) return false;
+        tc_fence_after();
+        const uint64_t dv = dv0 + (uint64_t)(j % kVStages) * (uint64_t)(kTile >> 4);
+        const uint32_t d = tmem + kColO + x * 128, pa = tmem + kColS + x * 128;
+        tc_mma_ts(d, pa, dv, idesc_o, j > 0 ? 1u : 0u);
+#pragma unroll
+        for (int kk = 1; kk < kKT / 16; ++kk) tc_mma_ts(d, pa + kk * 8, dv + ((kk * kPage) >> 4), idesc_o, 1u);
+        tc_commit(&sh->pv_done[x]);
+        return true;
+      };
+      // S_X = Q_X K_t^T, once the P V that last read S_X's columns is done
+      auto qk = [&](int x, int t) -> bool {
+        if (t >= 1 && !wait_or_abort(&sh->pv_done[x], (t - 1) & 1, sh, a.err)) return false;
+        tc_fence_after();
+        const uint64_t dq = x ? dq1 : dq0, dk = dk0 + (uint64_t)(t % kKStages) * dk_stride;
+        const uint32_t d = tmem + kColS + x * 128;
+#pragma unroll
+        for (int ks = 0; ks < kD / 16; ++ks) {
+          const uint32_t off = ((ks >> 2) * kHalf + (ks & 3) * 32) >> 4;
+          const uint32_t koff = ((ks >> 2) * 1024 + (ks & 3) * 32) >> 4;
+          tc_mma_ss(d, dq + off, dk + koff, idesc_s, ks > 0 ? 1u : 0u);
+        }
+        tc_commit(&sh->s_full[x]);
+        return true;
+      };
+      // A stage's copies were written by other threads through the generic
+      // proxy; after its mbarrier completes, a proxy fence orders them before
+      // the tensor core's reads.
       auto landed = [&](uint64_t* full, uint32_t parity) -> bool {
         if (!wait_or_abort(full, parity, sh, a.err)) return false;
         fence_proxy_async_smem();
         return true;
       };
-      // S(t) = Q K_t^T into S[t%2], once the softmax has read S(t-2) from it
-      auto qk = [&](int t) -> bool {
-        if (!landed(&sh->full_k[t % kKStages], (t / kKStages) & 1)) return false;
-        if (t >= 2 && !wait_or_abort(&sh->s_free[t & 1], ((t - 2) >> 1) & 1, sh, a.err)) return false;
-        tc_fence_after();
-        const uint64_t dk = dk0 + (uint64_t)(t % kKStages) * dstage;
-        const uint32_t d = tmem + kColS + (t & 1) * 128;
-#pragma unroll
-        for (int ks = 0; ks < kD / 16; ++ks) {
-          const uint32_t off = ((ks >> 2) * kHalf + (ks & 3) * 32) >> 4;
-          tc_mma_ss(d, dq + off, dk + off, idesc_s, ks > 0 ? 1u : 0u);
-        }
-        tc_commit(&sh->s_full[t & 1]);
-        tc_commit(&sh->empty_k[t % kKStages]);
-        return true;
-      };
-      // O += P(j) V_j, once P(j) is written (P in TMEM, the A operand)
-      auto pv = [&](int j) -> bool {
-        if (!wait_or_abort(&sh->p_full[j & 1], (j >> 1) & 1, sh, a.err)) return false;
-        if (!landed(&sh->full_v[j % kVStages], (j / kVStages) & 1)) return false;
-        tc_fence_after();
-        const uint64_t dv = dv0 + (uint64_t)(j % kVStages) * dstage;
-        const uint32_t d = tmem + kColO, pa = tmem + kColP + (j & 1) * 64;
-        tc_mma_ts(d, pa, dv, idesc_o, j > 0 ? 1u : 0u);
-#pragma unroll
-        for (int kk = 1; kk < kKT / 16; ++kk) tc_mma_ts(d, pa + kk * 8, dv + ((kk * 2048) >> 4), idesc_o, 1u);
-        tc_commit(&sh->pv_done[j & 1]);
-        tc_commit(&sh->empty_v[j % kVStages]);
-        return true;
-      };
-      // Issue order: S(0); then for t >= 1: S(t), P V(t-1); finally P V(last).
+      // Issue order per key tile t >= 1:  PV_A(t-1), S_A(t), PV_B(t-1), S_B(t),
+      // so tile A's softmax of t runs while the tensor pipe works on tile B.
       bool ok = wait_or_abort(&sh->q_full, 0, sh, a.err);
-      if (ok) {
-        tc_fence_after();
-        ok = qk(0);
+      if (ok) tc_fence_after();
+      if (ok && ntiles > 0) {
+        ok = landed(&sh->full_k[0], 0) && qk(0, 0) && qk(1, 0);
+        if (ok) tc_commit(&sh->empty_k[0]);
       }
-      for (int t = 1; t < ntiles && ok; ++t) ok = qk(t) && pv(t - 1);
-      if (ok) ok = pv(ntiles - 1);
+      for (int t = 1; t < ntiles && ok; ++t) {
+        const int j = t - 1;
+        ok = landed(&sh->full_v[j % kVStages], (j / kVStages) & 1) && pv(0, j) &&
+             landed(&sh->full_k[t % kKStages], (t / kKStages) & 1) && qk(0, t) && pv(1, j);
+        if (!ok) break;
+        tc_commit(&sh->empty_v[j % kVStages]);
+        if (!(ok = qk(1, t))) break;
+        tc_commit(&sh->empty_k[t % kKStages]);
+      }
+      if (ok && ntiles > 0) {
+        const int j = ntiles - 1;
+        ok = landed(&sh->full_v[j % kVStages], (j / kVStages) & 1) && pv(0, j) && pv(1, j);
+      }
       // every MMA issued here has finished before the CTA tears down
       tc_commit(&sh->mma_done);
       if (!mbar_wait(&sh->mma_done, 0)) raise_dev(a.err, BL_DEVERR_TIMEOUT);
     }
-  } else if (warp >= kSoftmaxWarp0) {
+  } else {
     // ------------------------------ softmax ------------------------------
-    const int grp = warp & 3;             // TMEM lane quadrant
-    const int r = 32 * grp + lane;        // row within the tile == TMEM lane
+    const int x = (warp - kSoftmaxWarp0) >> 2;  // tile: 0 = A, 1 = B
+    const int grp = warp & 3;             // TMEM lane group
+    const int tr = 32 * grp + lane;       // row within the tile == TMEM lane
+    const int r = x * kTileRows + tr;     // row within the CTA
     const uint32_t tl = tmem + ((uint32_t)(32 * grp) << 16);
+    const uint32_t sc = kColS + x * 128, oc = kColO + x * 128;
     const int hd = r / a.bq;
     const int tok = r - hd * a.bq;
     const int64_t qi = q0 + tok;
@@ -335,21 +366,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int hq = h * a.g + hd;
     const int64_t lim = prefix + qi;  // inclusive key limit
     // Q rows -> shared memory (K-major, 128-byte swizzle).  With 16-byte
-    // aligned rows the 128 softmax threads copy 16-byte chunks (a warp reads
+    // aligned rows the 256 softmax threads copy 16-byte chunks (a warp reads
     // two whole 256-byte rows at a time); rows past the chunk end are zeros.
     if (a.q_vec16) {
-      const int i = (warp - kSoftmaxWarp0) * 32 + lane;  // 0..127
+      const int i = (warp - kSoftmaxWarp0) * 32 + lane;  // 0..255
       const int qc = i & 15;
 #pragma unroll 4
       for (int k = 0; k < 16; ++k) {
-        const int row = (i >> 4) + 8 * k;
+        const int row = (i >> 4) + 16 * k;
         const int rhd = row / a.bq, rtok = row - rhd * a.bq;
         const int64_t rqi = q0 + rtok;
         const bool rvalid = rqi < nq;
         const T* src = reinterpret_cast<const T*>(a.q) + b * a.q_sb + (qo + (rvalid ? rqi : 0)) * a.q_st +
                        (int64_t)(h * a.g + rhd) * a.q_sh + qc * 8;
-        const uint32_t dst =
-            smem_u32(smem + kOffQ + (qc >> 3) * kHalf + row * 128 + (((qc & 7) ^ (row & 7)) << 4));
+        const int rt = row & (kTileRows - 1);
+        const uint32_t dst = smem_u32(smem + kOffQ + (row >> 7) * kTile + (qc >> 3) * kHalf + rt * 128 +
+                                      (((qc & 7) ^ (rt & 7)) << 4));
         asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(rvalid ? 16u : 0u)
                      : "memory");
       }
@@ -357,7 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
       const T* qrow = reinterpret_cast<const T*>(a.q) + b * a.q_sb + (qo + (valid ? qi : 0)) * a.q_st +
                       (int64_t)hq * a.q_sh;
-      unsigned char* qs = smem + kOffQ + r * 128;
+      unsigned char* qs = smem + kOffQ + x * kTile + tr * 128;
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
         uint4 v = make_uint4(0, 0, 0, 0);
@@ -365,7 +397,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t* src = reinterpret_cast<const uint32_t*>(qrow + c * 8);
           v = make_uint4(src[0], src[1], src[2], src[3]);
         }
-        *reinterpret_cast<uint4*>(qs + (c >> 3) * kHalf + (((c & 7) ^ (r & 7)) << 4)) = v;
+        *reinterpret_cast<uint4*>(qs + (c >> 3) * kHalf + (((c & 7) ^ (tr & 7)) << 4)) = v;
       }
     }
     fence_proxy_async_smem();
@@ -374,20 +406,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int t = 0; t < ntiles; ++t) {
-      const int x = t & 1;
-      ok = __all_sync(0xffffffffu, wait_or_abort(&sh->s_full[x], (t >> 1) & 1, sh, a.err));
+      ok = __all_sync(0xffffffffu, wait_or_abort(&sh->s_full[x], t & 1, sh, a.err));
       if (!ok) break;
       tc_fence_after();
       const int64_t k0 = (int64_t)t * kKT;
-      // the whole S row in registers: one TMEM read per tile, after which
-      // S[x] is free for S(t+2)
+      // the whole S row in registers: one TMEM read per tile
       float v[kKT];
 #pragma unroll
-      for (int c = 0; c < kKT / 32; ++c) tc_ld32f(tl + kColS + x * 128 + c * 32, v + c * 32);
+      for (int c = 0; c < kKT / 32; ++c) tc_ld32f(tl + sc + c * 32, v + c * 32);
       tc_wait_ld();
       reg_fence<kKT>(v);
-      tc_fence_before();
-      mbar_arrive(&sh->s_free[x]);
       // bottom-right causal mask: keys past `lim` drop out (only tiles that
       // cross the diagonal or the chunk end take this branch)
       const int64_t lim_rel64 = lim - k0;
@@ -409,30 +437,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float alpha = need ? fast_exp2(m_used - m_new) : 1.f;
       if (need || t == 0) m_used = m_new;
       const float ms = (m_used == -INFINITY) ? 0.f : m_used;
-      // P[x] was last read by P V(t-2)
-      if (t >= 2) {
-        ok = __all_sync(0xffffffffu, wait_or_abort(&sh->pv_done[x], ((t - 2) >> 1) & 1, sh, a.err));
-        if (!ok) break;
-      }
-      // lazy rescale of O, once P V(t-1) has landed in it; rare once the
-      // running max has settled
-      if (__any_sync(0xffffffffu, need)) {
-        ok = __all_sync(0xffffffffu, wait_or_abort(&sh->pv_done[x ^ 1], ((t - 1) >> 1) & 1, sh, a.err));
-        if (!ok) break;
-        tc_fence_after();
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          float o[32];
-          tc_ld32f(tl + kColO + c * 32, o);
-          tc_wait_ld();
-          reg_fence<32>(o);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) o[j] *= alpha;
-          tc_st32f(tl + kColO + c * 32, o);
-        }
-      }
-      tc_fence_after();
-      // P = exp2(s * scale - m), packed two per column into P[x]
+      // P = exp2(s * scale - m), packed two per column over S's first 64
+      // columns (S is already in registers)
       float rp[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < kKT / 32; ++c) {
@@ -444,9 +450,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           rp[j & 3] += p0 + p1;
           pk[j] = pack2<T>(p0, p1);
         }
-        tc_st16(tl + kColP + x * 64 + c * 16, pk);
+        tc_st16(tl + sc + c * 16, pk);
       }
       const float rs = (rp[0] + rp[1]) + (rp[2] + rp[3]);
+      // lazy rescale of O (the P V that last wrote O_X completed before S_X was
+      // issued); rare once the running max has settled
+      if (__any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float o[32];
+          tc_ld32f(tl + oc + c * 32, o);
+          tc_wait_ld();
+          reg_fence<32>(o);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) o[j] *= alpha;
+          tc_st32f(tl + oc + c * 32, o);
+        }
+      }
       tc_wait_st();
       l = l * alpha + rs;
       tc_fence_before();
@@ -454,8 +474,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     // ---- epilogue ----
     if (ok && ntiles > 0) {
-      const int j = ntiles - 1;
-      ok = __all_sync(0xffffffffu, wait_or_abort(&sh->pv_done[j & 1], (j >> 1) & 1, sh, a.err));
+      ok = __all_sync(0xffffffffu, wait_or_abort(&sh->pv_done[x], (ntiles - 1) & 1, sh, a.err));
       if (ok) {
         tc_fence_after();
         const float inv = l > 0.f ? 1.f / l : 0.f;
@@ -463,13 +482,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           float o[32];
-          tc_ld32f(tl + kColO + c * 32, o);
+          tc_ld32f(tl + oc + c * 32, o);
           tc_wait_ld();
           reg_fence<32>(o);
           if (valid) {
 #pragma unroll
-            for (int j2 = 0; j2 < 16; ++j2)
-              reinterpret_cast<uint32_t*>(orow + c * 32)[j2] = pack2<T>(o[2 * j2] * inv, o[2 * j2 + 1] * inv);
+            for (int j = 0; j < 16; ++j)
+              reinterpret_cast<uint32_t*>(orow + c * 32)[j] = pack2<T>(o[2 * j] * inv, o[2 * j + 1] * inv);
           }
         }
       }
@@ -520,7 +539,7 @@ int launch(const bl_prefill_args& a, cudaStream_t s) {
   k.max_q = a.max_q_len;
   const uint64_t rows = (uint64_t)a.kv.num_layers * a.kv.num_blocks * a.kv.num_kv_heads * kBS;
   CUtensorMap kmap, vmap;
-  if (!get_pool_tmap(a.kv.k_pool, rows, a.kv.dtype, &kmap) || !get_pool_tmap(a.kv.v_pool, rows, a.kv.dtype, &vmap))
+  if (!get_pool_page_tmap(a.kv.k_pool, rows, a.kv.dtype, &kmap) || !get_pool_page_tmap(a.kv.v_pool, rows, a.kv.dtype, &vmap))
     return BL_ERR_LAUNCH;
   k.rows_total = (int32_t)rows;
   k.q_vec16 = ((uintptr_t)a.q % 16 == 0) && a.q_stride_b % 8 == 0 && a.q_stride_t % 8 == 0 && a.q_stride_h % 8 == 0;
