@@ -15,6 +15,8 @@ runs differ only in the attention backend and cache.  Only tests may use it.
 
 from __future__ import annotations
 
+import math
+
 import torch
 import torch.nn.functional as F
 
@@ -89,9 +91,20 @@ class SDPAContiguousBackend:
 
 
 @torch.inference_mode()
+def _spacing(x: float, dtype: torch.dtype) -> float:
+    """The gap between adjacent representable values of ``dtype`` at |x|
+    (the logits' rounding step); 0 for float32, where margins stay absolute."""
+    mant = {torch.bfloat16: 7, torch.float16: 10}.get(dtype)
+    if mant is None:
+        return 0.0
+    return 2.0 ** (math.floor(math.log2(max(abs(x), 2.0 ** -14))) - mant)
+
+
 def generate_contiguous(model, prompts: list[list[int]], max_new_tokens: int, record_margins: bool = False):
     """Per-request prefill, then batched greedy decode, over contiguous caches.
-    Returns (new tokens per request, top-2 logit margins per step per request)."""
+    Returns (new tokens per request, top-2 logit margins per step per request);
+    with 16-bit logits a margin is counted in rounding steps of the top logit
+    (2 means the two best logits are two representable values apart)."""
     dev = next(model.parameters()).device
     saved = model.backend
     model.set_backend(SDPAContiguousBackend())
@@ -102,8 +115,12 @@ def generate_contiguous(model, prompts: list[list[int]], max_new_tokens: int, re
 
         def pick(logits_row):
             if record_margins:
+                # top-2 margin in units of the logits' rounding step at the top
+                # value (16-bit logits), or absolute (float32 logits)
                 top = torch.topk(logits_row.float(), 2).values
-                return int(torch.argmax(logits_row).item()), float(top[0] - top[1])
+                gap = float(top[0] - top[1])
+                step = _spacing(float(top[0]), logits_row.dtype)
+                return int(torch.argmax(logits_row).item()), (gap / step if step > 0 else gap)
             return int(torch.argmax(logits_row).item()), 0.0
 
         for i, c in enumerate(caches):

@@ -8,12 +8,16 @@ tests/test_batched_kv_cache.py:92-150), including at the Qwen3-0.6B
 architecture's full size (28 layers, vocab 151936).  bf16: teacher-forced --
 both runs are fed the oracle's own greedy tokens, and at every step of every
 prompt the paged run's argmax must equal the oracle's, except where the
-oracle's top-2 logits are a near-tie (bf16 logits round at ~1e-2 here); the
-number of such steps is small and reported.  The weights use the "spread"
+oracle's top-2 logits are a near-tie: at most 4 rounding steps of the bf16
+logits apart (the paged and the contiguous runs round their attention
+outputs differently, and the difference reaches the logits through the
+remaining layers as a few steps at most).  The weights use the "spread"
 random init, whose greedy streams do not collapse onto one repeated token
 (the tests check that)."""
 
 from __future__ import annotations
+
+import os
 
 import numpy as np
 import pytest
@@ -101,10 +105,14 @@ def paged_forced_argmax(model, prompts: list[list[int]], forced: list[list[int]]
     return got
 
 
-def forced_agreement(got, want, margins, tie: float):
-    """Steps where the argmax differs; each must be a near-tie of the oracle."""
+TIE_STEPS = 4.0  # a near-tie: the oracle's top-2 logits at most 4 bf16 rounding steps apart
+
+
+def forced_agreement(got, want, margins, tie: float = TIE_STEPS):
+    """Steps where the argmax differs; each must be a near-tie of the oracle
+    (``margins`` in rounding steps of the logits, from generate_contiguous)."""
     diffs = [(i, k, margins[i][k]) for i in range(len(want)) for k in range(len(want[i])) if got[i][k] != want[i][k]]
-    bad = [d for d in diffs if d[2] >= tie]
+    bad = [d for d in diffs if d[2] > tie + 1e-6]
     return diffs, bad
 
 
@@ -116,7 +124,7 @@ def test_bf16_teacher_forced_every_step_matches_up_to_near_ties(cuda, native_lib
     want, margins = generate_contiguous(model, prompts, n_new, record_margins=True)
     assert all(len(set(t)) >= 4 for t in want), want  # varied greedy streams
     got = paged_forced_argmax(model, prompts, want)
-    diffs, bad = forced_agreement(got, want, margins, tie=0.05)
+    diffs, bad = forced_agreement(got, want, margins)
     assert not bad, f"argmax differs away from a near-tie (prompt, step, oracle top-2 margin): {bad}"
     assert len(diffs) <= len(prompts) * n_new // 20, diffs
     # free-running greedy through the engine's CUDA-graph decode agrees with
@@ -126,7 +134,7 @@ def test_bf16_teacher_forced_every_step_matches_up_to_near_ties(cuda, native_lib
     for g, w, m in zip(free, want, margins):
         if g != w:
             k = next(i for i, (a, b) in enumerate(zip(g, w)) if a != b)
-            assert m[k] < 0.05, f"free-running divergence at step {k}, oracle top-2 margin {m[k]:.4f}"
+            assert m[k] <= TIE_STEPS, f"free-running divergence at step {k}, oracle top-2 margin {m[k]:.1f} steps"
 
 
 def test_qwen06b_full_architecture_fp32_greedy_identical(cuda, native_lib):
@@ -159,7 +167,7 @@ def test_qwen06b_full_architecture_bf16_teacher_forced(cuda, native_lib):
     want, margins = generate_contiguous(model, prompts, n_new, record_margins=True)
     assert all(len(set(t)) >= 4 for t in want)
     got = paged_forced_argmax(model, prompts, want)
-    diffs, bad = forced_agreement(got, want, margins, tie=0.05)
+    diffs, bad = forced_agreement(got, want, margins)
     assert not bad, f"argmax differs away from a near-tie (prompt, step, oracle top-2 margin): {bad}"
     assert len(diffs) <= len(prompts) * n_new // 20, diffs
 
@@ -178,3 +186,33 @@ def test_fp32_packed_chunked_prefill_matches_per_request_prefill(cuda, native_li
     single = PagedEngine(model, num_blocks=blocks, prefill_tokens=0).generate(prompts, max_new_tokens=10)
     want, _ = generate_contiguous(model, prompts, 10)
     assert packed == single == want
+
+
+@pytest.mark.skipif(not os.environ.get("BARELLM_FULL_E2E"),
+                    reason="the whole end-to-end configuration takes minutes; set BARELLM_FULL_E2E=1 to run it")
+def test_qwen06b_whole_configuration_bf16_teacher_forced(cuda, native_lib):
+    """The end-to-end configuration at its stated size: Qwen3-0.6B
+    architecture, bf16, all 128 prompts of U{64..2048} random token ids (the
+    bench's seed), 256 decode steps each, teacher-forced against the
+    contiguous-cache oracle; every step's argmax equals the oracle's except at
+    near-ties.  Prints the count and the margins of the steps that differ.
+    (With random weights and a 151936-token vocabulary the two best logits are
+    often within a few rounding steps, so the share of near-ties is a property
+    of the model, not a bar; the bar is that no step differs elsewhere.)"""
+    from barellm_b200.engine import QWEN3_06B
+
+    model = random_qwen3(QWEN3_06B, dtype=torch.bfloat16, device=cuda, seed=0)
+    rs = np.random.RandomState(2024)
+    lens = rs.randint(64, 2048 + 1, size=128)
+    prompts = [list(rs.randint(0, QWEN3_06B.vocab_size, size=int(n))) for n in lens]
+    n_new = 256
+    want, margins = generate_contiguous(model, prompts, n_new, record_margins=True)
+    assert all(len(set(t)) >= 4 for t in want)
+    got = paged_forced_argmax(model, prompts, want)
+    diffs, bad = forced_agreement(got, want, margins)
+    from collections import Counter
+
+    hist = sorted(Counter(round(d[2], 1) for d in diffs).items())
+    print(f"\nwhole configuration: {len(prompts)} prompts x {n_new} steps = {len(prompts) * n_new} steps, "
+          f"{len(diffs)} differ; oracle top-2 margin there, in bf16 rounding steps: count = {hist}")
+    assert not bad, f"argmax differs away from a near-tie (prompt, step, oracle top-2 margin): {bad}"
