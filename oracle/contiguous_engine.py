@@ -90,7 +90,6 @@ class SDPAContiguousBackend:
         return F.scaled_dot_product_attention(q, key, value, attn_mask=mask, is_causal=mask is None and q.shape[2] > 1)
 
 
-@torch.inference_mode()
 def _spacing(x: float, dtype: torch.dtype) -> float:
     """The gap between adjacent representable values of ``dtype`` at |x|
     (the logits' rounding step); 0 for float32, where margins stay absolute."""
@@ -100,6 +99,7 @@ def _spacing(x: float, dtype: torch.dtype) -> float:
     return 2.0 ** (math.floor(math.log2(max(abs(x), 2.0 ** -14))) - mant)
 
 
+@torch.inference_mode()
 def generate_contiguous(model, prompts: list[list[int]], max_new_tokens: int, record_margins: bool = False):
     """Per-request prefill, then batched greedy decode, over contiguous caches.
     Returns (new tokens per request, top-2 logit margins per step per request);
