@@ -318,12 +318,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_commit(&sh->s_full[x]);
         return true;
       };
-      // A stage's copies were written by other threads through the generic
-      // proxy; after its mbarrier completes, a proxy fence orders them before
-      // the tensor core's reads.
-      auto landed = [&](uint64_t* full, uint32_t parity) -> bool {
-        if (!wait_or_abort(full, parity, sh, a.err)) return false;
-        fence_proxy_async_smem();
+      // K stages are written by TMA only (the async proxy the tensor core
+      // reads through); a V stage also holds the row's partial last page when
+      // it ends inside that tile, written by cp.async (generic proxy): only
+      // then does the issuer need a proxy fence after the stage's barrier.
+      const int64_t part_lb = (len % kBS) ? (len - 1) / kBS : -1;
+      auto landed_k = [&](int t) -> bool {
+        return wait_or_abort(&sh->full_k[t % kKStages], (t / kKStages) & 1, sh, a.err);
+      };
+      auto landed_v = [&](int j) -> bool {
+        if (!wait_or_abort(&sh->full_v[j % kVStages], (j / kVStages) & 1, sh, a.err)) return false;
+        if (part_lb >= (int64_t)j * kPPT && part_lb < (int64_t)j * kPPT + kPPT) fence_proxy_async_smem();
         return true;
       };
       // Issue order per key tile t >= 1:  PV_A(t-1), S_A(t), PV_B(t-1), S_B(t),
@@ -331,13 +336,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = wait_or_abort(&sh->q_full, 0, sh, a.err);
       if (ok) tc_fence_after();
       if (ok && ntiles > 0) {
-        ok = landed(&sh->full_k[0], 0) && qk(0, 0) && qk(1, 0);
+        ok = landed_k(0) && qk(0, 0) && qk(1, 0);
         if (ok) tc_commit(&sh->empty_k[0]);
       }
       for (int t = 1; t < ntiles && ok; ++t) {
         const int j = t - 1;
-        ok = landed(&sh->full_v[j % kVStages], (j / kVStages) & 1) && pv(0, j) &&
-             landed(&sh->full_k[t % kKStages], (t / kKStages) & 1) && qk(0, t) && pv(1, j);
+        ok = landed_v(j) && pv(0, j) && landed_k(t) && qk(0, t) && pv(1, j);
         if (!ok) break;
         tc_commit(&sh->empty_v[j % kVStages]);
         if (!(ok = qk(1, t))) break;
@@ -345,7 +349,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (ok && ntiles > 0) {
         const int j = ntiles - 1;
-        ok = landed(&sh->full_v[j % kVStages], (j / kVStages) & 1) && pv(0, j) && pv(1, j);
+        ok = landed_v(j) && pv(0, j) && pv(1, j);
       }
       // every MMA issued here has finished before the CTA tears down
       tc_commit(&sh->mma_done);
