@@ -330,6 +330,28 @@ __global__ void __launch_bounds__(kWarps * 32, E <= 8 ? 4 : 2) qk_prep_kernel(co
     for (int i = 0; i < kTok; ++i)
       if (t0 + i < t_end) xr[i] = load_raw<T, E, VEC>(src + (int64_t)(t0 + i) * src_st);
   }
+  // The block's tokens fall into at most two pages when the block size is at
+  // least the token tile: their block-table entries are read here, once and
+  // early (their latency overlaps the row loads and the cos / sin staging),
+  // instead of one dependent table read per token before its store.
+  const int32_t start = a.start_pos[b];
+  const int64_t row = a.row_ids ? (int64_t)a.row_ids[b] : b;
+  const int32_t* bt = a.block_tables + row * a.bt_stride;
+  int32_t lb_first = 0, lb_last = -1;
+  int64_t ph_first = -1, ph_last = -1;
+  if (active && kind != 0) {
+    const int32_t p0 = start + t0, p1 = start + t_end - 1;
+    if (p0 >= 0) {
+      lb_first = a.bs_shift >= 0 ? (p0 >> a.bs_shift) : p0 / a.bs;
+      lb_last = a.bs_shift >= 0 ? (p1 >> a.bs_shift) : p1 / a.bs;
+      if (lb_last - lb_first <= 1) {
+        if (lb_first < a.bt_width) ph_first = bt[lb_first];
+        if (lb_last != lb_first && lb_last < a.bt_width) ph_last = bt[lb_last];
+      } else {
+        lb_last = -1;  // more than two pages: per-token reads below
+      }
+    }
+  }
   // cos / sin rows of the block's tokens into shared memory
   {
     const int n = (t_end - t0) * D;
@@ -353,9 +375,6 @@ __global__ void __launch_bounds__(kWarps * 32, E <= 8 ? 4 : 2) qk_prep_kernel(co
   }
   T* qo = reinterpret_cast<T*>(a.q_out) + bi * a.qo_sb + (int64_t)h * a.qo_sh + E * sub;
   T* pool = reinterpret_cast<T*>(kind == 1 ? a.k_pool : a.v_pool);
-  const int64_t row = a.row_ids ? (int64_t)a.row_ids[b] : b;
-  const int32_t* bt = a.block_tables + row * a.bt_stride;
-  const int32_t start = a.start_pos[b];
 
   for (int tt = t0; tt < t_end; tt += kTok) {
     if (tt != t0) {
@@ -403,7 +422,7 @@ __global__ void __launch_bounds__(kWarps * 32, E <= 8 ? 4 : 2) qk_prep_kernel(co
         if (sub == 0) raise_dev(a.err, BL_DEVERR_TABLE);
         continue;
       }
-      const int64_t phys = bt[lb];
+      const int64_t phys = lb == lb_first && lb_last >= 0 ? ph_first : (lb == lb_last ? ph_last : bt[lb]);
       if (phys < 0 || phys >= a.num_blocks) {
         if (sub == 0) raise_dev(a.err, BL_DEVERR_BLOCK_ID);
         continue;
