@@ -555,6 +555,8 @@ struct ReduceArgs {
   int32_t max_units;
 };
 
+constexpr int kReduceMaxChunks = 1024;  // chunks whose weights the reduce keeps in shared memory
+
 // grid (batch, hq); block = d threads
 template <typename T>
 __global__ void __launch_bounds__(256) decode_reduce_kernel(const ReduceArgs a) {
@@ -569,17 +571,53 @@ __global__ void __launch_bounds__(256) decode_reduce_kernel(const ReduceArgs a) 
   if (nch <= 1) return;
   const int64_t base = a.row_base[b];
   if (base < 0 || base + nch > a.max_units) return;  // plan overflow, flagged by the plan kernel
-  float M = -INFINITY;
-  for (int c = 0; c < nch; ++c) M = fmaxf(M, a.ws_lse[(base + c) * a.hq + hq]);
-  // blockDim.x == a.d: one output element per thread
+  // blockDim.x == a.d == kD (four warps): one output element per thread
   __shared__ __align__(16) T s_out[kD];
+  __shared__ float s_w[kReduceMaxChunks];
+  __shared__ float s_red[kD / 32];
   const int d = threadIdx.x;
   float num = 0.f, den = 0.f;
-  for (int c = 0; c < nch; ++c) {
-    const float lse = a.ws_lse[(base + c) * a.hq + hq];
-    const float w = (lse == -INFINITY) ? 0.f : fast_exp2(lse - M);
-    num += w * a.ws_o[((base + c) * a.hq + hq) * a.d + d];
-    den += w;
+  if (nch <= kReduceMaxChunks) {
+    // The chunks' log-sum-exps are read once, by all threads at the same
+    // time, and their weights kept in shared memory; each thread then sums its
+    // dimension over the chunks with independent loads.  (Reading them chunk
+    // by chunk in every thread made the reduce a chain of dependent global
+    // loads.)  The arithmetic and its order are those of the plain loop below.
+    float mloc = -INFINITY;
+    for (int c = d; c < nch; c += kD) {
+      const float l = a.ws_lse[(base + c) * a.hq + hq];
+      s_w[c] = l;
+      mloc = fmaxf(mloc, l);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, o));
+    if ((d & 31) == 0) s_red[d >> 5] = mloc;
+    __syncthreads();
+    float M = s_red[0];
+#pragma unroll
+    for (int w = 1; w < kD / 32; ++w) M = fmaxf(M, s_red[w]);
+    for (int c = d; c < nch; c += kD) {
+      const float l = s_w[c];
+      s_w[c] = (l == -INFINITY) ? 0.f : fast_exp2(l - M);
+    }
+    __syncthreads();
+    const float* po = a.ws_o + (base * a.hq + hq) * a.d + d;
+    const int64_t cstride = (int64_t)a.hq * a.d;
+#pragma unroll 8
+    for (int c = 0; c < nch; ++c) {
+      const float w = s_w[c];
+      num += w * po[c * cstride];
+      den += w;
+    }
+  } else {
+    float M = -INFINITY;
+    for (int c = 0; c < nch; ++c) M = fmaxf(M, a.ws_lse[(base + c) * a.hq + hq]);
+    for (int c = 0; c < nch; ++c) {
+      const float lse = a.ws_lse[(base + c) * a.hq + hq];
+      const float w = (lse == -INFINITY) ? 0.f : fast_exp2(lse - M);
+      num += w * a.ws_o[((base + c) * a.hq + hq) * a.d + d];
+      den += w;
+    }
   }
   const T val = from_f32<T>(den > 0.f ? num / den : 0.f);
   const int64_t row = (int64_t)b * a.o_sb + (int64_t)hq * a.o_sh;
