@@ -340,8 +340,8 @@ def traffic_from_profile(kernel: str, workload: str, algorithmic_bytes: float | 
 def e2e_measure(wl: dict, work: DecodeWorkload, steps: int, warmup: int, device) -> dict:
     """The same metric through the public API (PagedKVCache + BatchKVCache +
     CudaPagedAttentionBackend.attend) with host-resident inputs: each step
-    copies q / k / v from pinned host memory, appends + attends, and copies the
-    output back."""
+    copies q / k / v from pinned host memory (one copy of a packed buffer),
+    appends + attends, and copies the output back."""
     from barellm_b200 import BatchKVCache, BlockPool, CudaPagedAttentionBackend, KVCacheManager, PagedKVCache, ops
 
     hq, hkv, d, bs = wl["hq"], wl["hkv"], wl["d"], wl["bs"]
@@ -371,19 +371,19 @@ def e2e_measure(wl: dict, work: DecodeWorkload, steps: int, warmup: int, device)
         vw.layer(0).append_only(kd, vd)
         del kd, vd
     backend = CudaPagedAttentionBackend()
-    q_h = work.q.cpu().pin_memory()
-    k_h = work.k_new.cpu().pin_memory()
-    v_h = work.v_new.cpu().pin_memory()
+    # the step's q, k and v side by side in one pinned host buffer, so one
+    # host-to-device copy brings them all; the device tensors are views
+    nq, nk = work.q.numel(), work.k_new.numel()
+    in_h = torch.cat([work.q.reshape(-1), work.k_new.reshape(-1), work.v_new.reshape(-1)]).cpu().pin_memory()
+    in_d = torch.empty_like(in_h, device=device)
+    q_d = in_d[:nq].view(work.q.shape)
+    k_d = in_d[nq : nq + nk].view(work.k_new.shape)
+    v_d = in_d[nq + nk :].view(work.v_new.shape)
     out_h = torch.empty((b, hq, 1, d), dtype=torch.bfloat16).pin_memory()
-    q_d = torch.empty_like(work.q)
-    k_d = torch.empty_like(work.k_new)
-    v_d = torch.empty_like(work.v_new)
     seq_hist: list[list[int]] = []
 
     def one():
-        q_d.copy_(q_h, non_blocking=True)
-        k_d.copy_(k_h, non_blocking=True)
-        v_d.copy_(v_h, non_blocking=True)
+        in_d.copy_(in_h, non_blocking=True)
         layer = BatchKVCache(views).layer(0)
         out = backend.attend(q_d, k_d, v_d, layer, hq // hkv)
         seq_hist.append(layer.starts().tolist())
@@ -396,7 +396,7 @@ def e2e_measure(wl: dict, work: DecodeWorkload, steps: int, warmup: int, device)
     ms = time_steps(one, steps, device)
     kv.check_device_errors()
     nbytes = sum(work.decode_bytes(s) for s in seq_hist)
-    h2d = (q_h.numel() + k_h.numel() + v_h.numel()) * 2 + 3 * b * 4
+    h2d = in_h.numel() * 2 + 3 * b * 4
     d2h = out_h.numel() * 2
     return {"ms": ms, "bytes": nbytes, "h2d": h2d, "d2h": d2h}
 
@@ -1018,16 +1018,16 @@ def run_heads(args, wl_name: str) -> None:
     # end to end through the public API: this GPU's q / new K / new V heads
     # from pinned host memory, append + sharded decode, the gathered
     # [B, Hq, D] output back to the host
-    q_h = work.q.cpu().pin_memory()
-    k_h = work.k_new.cpu().pin_memory()
-    v_h = work.v_new.cpu().pin_memory()
+    nq, nk = work.q.numel(), work.k_new.numel()
+    in_h = torch.cat([work.q.reshape(-1), work.k_new.reshape(-1), work.v_new.reshape(-1)]).cpu().pin_memory()
+    in_d = torch.empty_like(in_h, device=device)  # one copy brings q, k and v; views below
+    q_d = in_d[:nq].view(work.q.shape)
+    k_d = in_d[nq : nq + nk].view(work.k_new.shape)
+    v_d = in_d[nq + nk :].view(work.v_new.shape)
     out_h = torch.empty((work.batch, hq, d), dtype=torch.bfloat16).pin_memory()
-    q_d, k_d, v_d = torch.empty_like(work.q), torch.empty_like(work.k_new), torch.empty_like(work.v_new)
 
     def e2e_step():
-        q_d.copy_(q_h, non_blocking=True)
-        k_d.copy_(k_h, non_blocking=True)
-        v_d.copy_(v_h, non_blocking=True)
+        in_d.copy_(in_h, non_blocking=True)
         ops.paged_append(work.k_cache, work.v_cache, 0, work.bt, work.starts, k_d, v_d, err=work.err)
         out = work.shard.decode(q_d, work.k_cache, work.v_cache, 0, work.bt, work.seq_lens, work.max_seq,
                                 ws=work.ws, err=work.err)
@@ -1097,7 +1097,7 @@ def run_heads(args, wl_name: str) -> None:
             "cpu_baseline": cpu,
             "cpu_baseline_port": cpu_port,
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
-                    "h2d_bytes_per_step": (q_h.numel() + k_h.numel() + v_h.numel()) * 2,
+                    "h2d_bytes_per_step": in_h.numel() * 2,
                     "d2h_bytes_per_step": out_h.numel() * 2, "ms_per_step": e2e_ms_max / steps,
                     "path": "ops.paged_append + HeadShardedDecode.decode, pinned host I/O per GPU"},
             "gpu_launches": 5 * steps,
