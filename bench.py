@@ -346,7 +346,7 @@ def e2e_measure(wl: dict, work: DecodeWorkload, steps: int, warmup: int, device)
 
     hq, hkv, d, bs = wl["hq"], wl["hkv"], wl["d"], wl["bs"]
     b = work.batch
-    total_steps = steps + warmup
+    total_steps = 2 * steps + warmup  # the timed steps, the warm-up and the host-issue timing
     need = sum(-(-(n + total_steps + 1) // bs) for n in work.lens)
     pool_blocks = min(work.pool_blocks, int(need * 1.05) + 64)
     kv = PagedKVCache(1, pool_blocks, hkv, bs, d, dtype=torch.bfloat16, device=device, max_requests=b)
@@ -398,7 +398,15 @@ def e2e_measure(wl: dict, work: DecodeWorkload, steps: int, warmup: int, device)
     nbytes = sum(work.decode_bytes(s) for s in seq_hist)
     h2d = in_h.numel() * 2 + 3 * b * 4
     d2h = out_h.numel() * 2
-    return {"ms": ms, "bytes": nbytes, "h2d": h2d, "d2h": d2h}
+    # the host's own time to issue a step (outside the timed region): when it
+    # is close to the device step, the public-API step is host-bound
+    torch.cuda.synchronize(device)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        one()
+    host_ms = (time.perf_counter() - t0) * 1e3 / steps
+    torch.cuda.synchronize(device)
+    return {"ms": ms, "bytes": nbytes, "h2d": h2d, "d2h": d2h, "host_issue_ms": host_ms}
 
 
 def cpu_sample_state(wl: dict, lens: list[int], seed: int = 5):
@@ -763,6 +771,7 @@ def run_ours(args, wl_name: str) -> None:
             "cpu_baseline_port": cpu_port,
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": e2e["h2d"],
                     "d2h_bytes_per_step": e2e["d2h"], "ms_per_step": e2e_ms / steps,
+                    "host_issue_ms_per_step": round(e2e["host_issue_ms"], 4),
                     "path": "PagedKVCache + BatchKVCache + CudaPagedAttentionBackend.attend, pinned host I/O"},
             "gpu_launches": 4 * steps,
             "clocks": sampler.summary(),
