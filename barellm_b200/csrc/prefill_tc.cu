@@ -30,15 +30,19 @@
 //               O_B 384..511) and, on one lane, the MMA issuer.  Per key tile t
 //               it issues O_A += P_A V_{t-1}, S_A = Q_A K_t^T, O_B += P_B V_{t-1},
 //               S_B = Q_B K_t^T, so one tile's softmax runs while the tensor
-//               pipe works on the other tile.  S_X is rewritten only after the
-//               P V that read P_X (stored in S_X's columns) has completed.
+//               pipe works on the other tile.  S_X(t) is issued right behind
+//               the P V that reads P_X from S_X's columns, without waiting for
+//               it: the tensor pipe runs one thread's MMAs in issue order (the
+//               ordering CUTLASS's Blackwell FMHA mainloop also relies on), so
+//               the overwrite follows the read.
 //   warps 4..7  softmax of tile A, warps 8..11 of tile B: one thread per score
 //               row (= TMEM lane).  The S row is read from TMEM once into
 //               registers (bottom-right causal mask, row max in log2 units),
 //               exponentiated and written back as packed bf16/fp16 P over the
 //               first 64 S columns, where the P V MMA reads it as its A
 //               operand; a lazy rescale touches O only when the running max
-//               grows by more than 2^8.  Epilogue: O / l from TMEM to global.
+//               grows by more than 2^8.  Epilogue: O / l from TMEM, staged in
+//               Q's shared memory and written back as whole 256-byte rows.
 // Every mbarrier wait is bounded; on a time-out the CTA records
 // BL_DEVERR_TIMEOUT, drains what it issued and frees its TMEM.
 // Roofline: tensor.  Algorithmic flops per request: 4 * Hq * D * (C*P + C(C+1)/2).
@@ -88,6 +92,7 @@ struct Args {
   const uint16_t* k_pool;
   const uint16_t* v_pool;
   int32_t q_vec16;  // q rows start on 16-byte boundaries (pointer and strides)
+  int32_t o_vec16;  // out rows start on 16-byte boundaries (pointer and strides)
   int32_t rows_total;  // rows of the K tensor map: an out-of-range row coordinate
   int32_t hkv, g, bq;  // bq = query tokens per CTA = kRows / g
   int64_t num_blocks, layer_row0, max_q;
@@ -300,13 +305,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_mma_ts(d, pa, dv, idesc_o, j > 0 ? 1u : 0u);
 #pragma unroll
         for (int kk = 1; kk < kKT / 16; ++kk) tc_mma_ts(d, pa + kk * 8, dv + ((kk * kPage) >> 4), idesc_o, 1u);
-        tc_commit(&sh->pv_done[x]);
+        if (j == ntiles - 1) tc_commit(&sh->pv_done[x]);  // O_X final: the epilogue's signal
         return true;
       };
-      // S_X = Q_X K_t^T, once the P V that last read S_X's columns is done
+      // S_X = Q_X K_t^T, queued behind the P V that last read S_X's columns
       auto qk = [&](int x, int t) -> bool {
-        if (t >= 1 && !wait_or_abort(&sh->pv_done[x], (t - 1) & 1, sh, a.err)) return false;
-        tc_fence_after();
         const uint64_t dq = x ? dq1 : dq0, dk = dk0 + (uint64_t)(t % kKStages) * dk_stride;
         const uint32_t d = tmem + kColS + x * 128;
 #pragma unroll
@@ -341,7 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       for (int t = 1; t < ntiles && ok; ++t) {
         const int j = t - 1;
-        ok = landed_v(j) && pv(0, j) && landed_k(t) && qk(0, t) && pv(1, j);
+        ok = landed_v(j) && landed_k(t) && pv(0, j) && qk(0, t) && pv(1, j);
         if (!ok) break;
         tc_commit(&sh->empty_v[j % kVStages]);
         if (!(ok = qk(1, t))) break;
@@ -457,8 +460,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_st16(tl + sc + c * 16, pk);
       }
       const float rs = (rp[0] + rp[1]) + (rp[2] + rp[3]);
-      // lazy rescale of O (the P V that last wrote O_X completed before S_X was
-      // issued); rare once the running max has settled
+      // lazy rescale of O (S_X's commit tracks every MMA issued before it, so
+      // the P V that last wrote O_X has completed); rare once the running max
+      // has settled
       if (__any_sync(0xffffffffu, need)) {
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
@@ -478,21 +482,60 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     // ---- epilogue ----
     if (ok && ntiles > 0) {
-      ok = __all_sync(0xffffffffu, wait_or_abort(&sh->pv_done[x], (ntiles - 1) & 1, sh, a.err));
+      ok = __all_sync(0xffffffffu, wait_or_abort(&sh->pv_done[x], 0, sh, a.err));
       if (ok) {
         tc_fence_after();
         const float inv = l > 0.f ? 1.f / l : 0.f;
-        T* orow = reinterpret_cast<T*>(a.out) + b * a.o_sb + (qo + (valid ? qi : 0)) * a.o_st + (int64_t)hq * a.o_sh;
+        if (a.o_vec16) {
+          // Every S MMA finished before the last P V of either tile (they were
+          // issued earlier by the same thread), so Q's shared memory is free:
+          // each warp stages its 32 rows there (16-byte chunks XOR-swizzled by
+          // row) and writes them back as whole 256-byte rows, two per store.
+          unsigned char* stage = smem + kOffQ + x * kTile + grp * (32 * kD * 2);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          float o[32];
-          tc_ld32f(tl + oc + c * 32, o);
-          tc_wait_ld();
-          reg_fence<32>(o);
-          if (valid) {
+          for (int c = 0; c < 4; ++c) {
+            float o[32];
+            tc_ld32f(tl + oc + c * 32, o);
+            tc_wait_ld();
+            reg_fence<32>(o);
 #pragma unroll
-            for (int j = 0; j < 16; ++j)
-              reinterpret_cast<uint32_t*>(orow + c * 32)[j] = pack2<T>(o[2 * j] * inv, o[2 * j + 1] * inv);
+            for (int k = 0; k < 4; ++k) {
+              const int ch = c * 4 + k;
+              uint4 w;
+              w.x = pack2<T>(o[8 * k + 0] * inv, o[8 * k + 1] * inv);
+              w.y = pack2<T>(o[8 * k + 2] * inv, o[8 * k + 3] * inv);
+              w.z = pack2<T>(o[8 * k + 4] * inv, o[8 * k + 5] * inv);
+              w.w = pack2<T>(o[8 * k + 6] * inv, o[8 * k + 7] * inv);
+              *reinterpret_cast<uint4*>(stage + lane * 256 + ((ch ^ (lane & 7)) << 4)) = w;
+            }
+          }
+          __syncwarp();
+          const int ch = lane & 15;
+#pragma unroll 4
+          for (int it = 0; it < 16; ++it) {
+            const int rl = 2 * it + (lane >> 4);  // row within the warp's 32
+            const int rr = x * kTileRows + 32 * grp + rl;
+            const int rhd = rr / a.bq;
+            const int64_t rqi = q0 + (rr - rhd * a.bq);
+            if (rqi < nq) {
+              const uint4 w = *reinterpret_cast<const uint4*>(stage + rl * 256 + ((ch ^ (rl & 7)) << 4));
+              T* dst = reinterpret_cast<T*>(a.out) + b * a.o_sb + (qo + rqi) * a.o_st + (int64_t)(h * a.g + rhd) * a.o_sh;
+              *reinterpret_cast<uint4*>(dst + ch * 8) = w;
+            }
+          }
+        } else {
+          T* orow = reinterpret_cast<T*>(a.out) + b * a.o_sb + (qo + (valid ? qi : 0)) * a.o_st + (int64_t)hq * a.o_sh;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            float o[32];
+            tc_ld32f(tl + oc + c * 32, o);
+            tc_wait_ld();
+            reg_fence<32>(o);
+            if (valid) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j)
+                reinterpret_cast<uint32_t*>(orow + c * 32)[j] = pack2<T>(o[2 * j] * inv, o[2 * j + 1] * inv);
+            }
           }
         }
       }
@@ -547,6 +590,8 @@ int launch(const bl_prefill_args& a, cudaStream_t s) {
     return BL_ERR_LAUNCH;
   k.rows_total = (int32_t)rows;
   k.q_vec16 = ((uintptr_t)a.q % 16 == 0) && a.q_stride_b % 8 == 0 && a.q_stride_t % 8 == 0 && a.q_stride_h % 8 == 0;
+  k.o_vec16 = ((uintptr_t)a.out % 16 == 0) && a.out_stride_b % 8 == 0 && a.out_stride_t % 8 == 0 &&
+              a.out_stride_h % 8 == 0;
   k.k_pool = static_cast<const uint16_t*>(a.kv.k_pool);
   k.v_pool = static_cast<const uint16_t*>(a.kv.v_pool);
   k.scale_log2 = a.scale * kLog2e;
