@@ -300,6 +300,25 @@ def test_prefill_rows_vs_oracle_full_workload(cuda, prefill_chunks):
         assert_close(ob[:, :, :8], ref)
 
 
+def test_prefill_repeat_launches_bitwise_identical_full_workload(cuda, prefill_chunks):
+    """The MMA issuer queues S_X behind the P V that reads P_X from S_X's own
+    TMEM columns without waiting for it (a thread's MMAs run in issue order).
+    Were that overwrite ever to overtake the read, outputs would change from
+    launch to launch; every launch of the full workload must give the same
+    bits."""
+    w = prefill_chunks
+    gen = torch.Generator(device=cuda)
+    gen.manual_seed(14)
+    kc, vc = fill_prefill_pool(
+        w, cuda,
+        lambda b, n: torch.randn((1, w["hkv"], n, D), generator=gen, device=cuda).to(torch.bfloat16),
+        lambda b, n: torch.randn((1, w["hkv"], n, D), generator=gen, device=cuda).to(torch.bfloat16))
+    first = run_prefill(w, kc, vc, cuda).clone()
+    assert torch.isfinite(first).all()
+    for _ in range(7):
+        assert torch.equal(run_prefill(w, kc, vc, cuda), first)
+
+
 def test_prefill_constant_v_full_workload(cuda, prefill_chunks):
     w = prefill_chunks
     gen = torch.Generator(device=cuda)
