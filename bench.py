@@ -1288,6 +1288,7 @@ def run_prefill(args, wl_name: str) -> None:
     att_ms = time_steps(work.attention, max(steps, 5), device) / max(steps, 5)
     peak, peak_src = load_peaks("bf16_tflops")
     achieved = work.flops / (att_ms / 1e3) / 1e12
+    traffic, traffic_note = traffic_from_profile("prefill_tc_kernel", wl_name)
     e2e = prefill_e2e(wl, work, steps, warmup, device)
     e2e_ms = allreduce(e2e["ms"], "max", world, device)
     e2e_value = flops_all * steps / (e2e_ms / 1e3) / 1e12
@@ -1321,7 +1322,8 @@ def run_prefill(args, wl_name: str) -> None:
             },
             "roofline": {"kernel": "prefill_tc_kernel", "bound": "tensor", "achieved": round(achieved, 2),
                          "peak": peak, "peak_source": f"{peak_src} bf16_tflops (cuBLAS burst)", "unit": "TFLOP/s",
-                         "frac": round(achieved / peak, 4), "traffic": None, "launch_ms": att_ms},
+                         "frac": round(achieved / peak, 4), "traffic": traffic, "traffic_note": traffic_note,
+                         "launch_ms": att_ms},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": e2e["h2d"],
                     "d2h_bytes_per_step": e2e["d2h"], "ms_per_step": e2e_ms / steps,
