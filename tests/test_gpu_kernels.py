@@ -299,6 +299,46 @@ def test_packed_chunked_prefill_many_requests(cuda, native_lib, hq, hkv, dtype):
         o += chunk
 
 
+@pytest.mark.parametrize("pad", [2, 8])
+def test_packed_prefill_strided_q_and_out_match_contiguous(cuda, native_lib, pad):
+    """q and out as views of [1, T, Hq, D + pad] buffers.  pad = 2 gives rows
+    that do not start on 16-byte boundaries (the kernel loads q and stores the
+    output element-wise); pad = 8 keeps 16-byte rows with non-default strides
+    (vector paths).  Either way the arithmetic is the same, so the output must
+    equal the contiguous call bit for bit."""
+    rs = np.random.RandomState(11)
+    specs = [(0, 45), (37, 130), (300, 17), (16, 200), (513, 64)]
+    hq, hkv, bs, D, P, dtype = 32, 8, 16, 128, 512, torch.bfloat16
+    kc = torch.full((1, P, hkv, bs, D), gh.SENTINEL, dtype=dtype, device=cuda)
+    vc = torch.full_like(kc, gh.SENTINEL)
+    free = list(rs.permutation(P))
+    tables, lens = [], []
+    for prefix, chunk in specs:
+        total = prefix + chunk
+        tables.append(np.array([free.pop() for _ in range((total + bs - 1) // bs)], dtype=np.int32))
+        lens.append(total)
+    bt = torch.from_numpy(gh.padded_tables(tables)).to(cuda)
+    gen = torch.Generator().manual_seed(11)
+    for b, (prefix, chunk) in enumerate(specs):
+        k = torch.randn(1, hkv, prefix + chunk, D, generator=gen).to(dtype).to(cuda)
+        v = torch.randn(1, hkv, prefix + chunk, D, generator=gen).to(dtype).to(cuda)
+        ops.paged_append(kc, vc, 0, bt[b : b + 1], torch.tensor([0], dtype=torch.int32, device=cuda), k, v)
+    T = sum(c for _, c in specs)
+    q = torch.randn(1, T, hq, D, generator=gen).to(dtype).to(cuda).transpose(1, 2)
+    offs = torch.tensor(np.concatenate([[0], np.cumsum([c for _, c in specs])]), dtype=torch.int32, device=cuda)
+    seq = torch.tensor(lens, dtype=torch.int32, device=cuda)
+    mq = max(c for _, c in specs)
+    want = ops.paged_prefill(q, kc, vc, 0, bt, seq, q_offsets=offs, max_q_len=mq)
+    qbuf = torch.zeros(1, T, hq, D + pad, dtype=dtype, device=cuda)
+    qbuf[..., :D] = q.transpose(1, 2)
+    obuf = torch.full((1, T, hq, D + pad), float("nan"), dtype=dtype, device=cuda)
+    got = ops.paged_prefill(qbuf[..., :D].transpose(1, 2), kc, vc, 0, bt, seq, q_offsets=offs, max_q_len=mq,
+                            out=obuf[..., :D].transpose(1, 2))
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+    assert torch.isnan(obuf[..., D:]).all()  # nothing written past each row
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_stale_nan_slots_never_reach_the_outputs(cuda, native_lib, dtype):
     """The pool starts as NaN everywhere (the reference never clears freed
